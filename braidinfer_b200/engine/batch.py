@@ -1,0 +1,152 @@
+"""Host-side planning of one forward pass: token inputs, KV write slots and the
+cascade attention plan, packed into ONE int32 buffer so a step costs a single
+host→device copy (and so CUDA-graph replays only refresh that buffer).
+
+The reference rebuilt page indices inside every attention layer with Python
+loops (``braidinfer/engine/page_manager.py:121-157``,
+``braidinfer/layers/attention.py:55-124``); here the plan is built once per
+step and shared by all layers.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import List, Optional
+
+import numpy as np
+import torch
+
+from ..ops.attention import AttnMeta
+from .sequence import SegmentRef
+
+FIELDS = ("input_ids", "positions", "slots", "qo_indptr", "seg_indptr", "seg_page_indptr",
+          "seg_offset", "seg_len", "seg_pos0", "seg_delta", "page_ids", "logits_idx")
+
+
+@dataclass
+class FwdItem:
+    tokens: List[int]
+    pos0: int                 # global position of tokens[0]
+    priv_index0: int          # private-token index of tokens[0]
+    priv_pages: List[int]
+    priv_pos0: int            # global position of private token 0
+    segments: List[SegmentRef] = field(default_factory=list)
+    logits: bool = True
+
+
+@dataclass
+class Plan:
+    arrays: dict
+    num_seqs: int
+    num_tokens: int
+    max_q_len: int
+    max_kv_len: int
+    decode: bool
+    sizes: dict
+
+
+def build_plan(items: List[FwdItem], page_size: int, pad_seqs: int = 0, scratch_page: int = 0,
+               seg_cap: Optional[int] = None, page_cap: Optional[int] = None) -> Plan:
+    """Flatten ``items`` into the kernel metadata.  ``pad_seqs`` appends dummy
+    one-token sequences (CUDA-graph padding) that write to ``scratch_page``."""
+    ids, pos, slots = [], [], []
+    qo, segi = [0], [0]
+    spi, soff, slen, spos0, sdelta, pids = [0], [], [], [], [], []
+    lidx = []
+    max_q = max_kv = 0
+    for it in items:
+        n = len(it.tokens)
+        t0 = len(ids)
+        ids.extend(it.tokens)
+        pos.extend(range(it.pos0, it.pos0 + n))
+        for k in range(it.priv_index0, it.priv_index0 + n):
+            slots.append(it.priv_pages[k // page_size] * page_size + k % page_size)
+        qo.append(len(ids))
+        kv = 0
+        for s in it.segments:
+            if s.length <= 0:
+                continue
+            npg = -(-(s.offset + s.length) // page_size)
+            pids.extend(s.pages[:npg])
+            spi.append(len(pids))
+            soff.append(s.offset)
+            slen.append(s.length)
+            spos0.append(s.pos0)
+            sdelta.append(s.delta)
+            kv += s.length
+        priv_len = it.priv_index0 + n
+        if priv_len > 0:
+            npg = -(-priv_len // page_size)
+            pids.extend(it.priv_pages[:npg])
+            spi.append(len(pids))
+            soff.append(0)
+            slen.append(priv_len)
+            spos0.append(it.priv_pos0)
+            sdelta.append(0)
+            kv += priv_len
+        segi.append(len(slen))
+        if it.logits and n > 0:
+            lidx.append(t0 + n - 1)
+        max_q = max(max_q, n)
+        max_kv = max(max_kv, kv)
+    for _ in range(pad_seqs):
+        ids.append(0)
+        pos.append(0)
+        slots.append(scratch_page * page_size)
+        qo.append(len(ids))
+        pids.append(scratch_page)
+        spi.append(len(pids))
+        soff.append(0)
+        slen.append(1)
+        spos0.append(0)
+        sdelta.append(0)
+        segi.append(len(slen))
+        lidx.append(len(ids) - 1)
+        max_q = max(max_q, 1)
+        max_kv = max(max_kv, 1)
+    S = len(slen)
+    if seg_cap is not None:
+        if S > seg_cap:
+            raise OverflowError("segment capacity")
+        pad = seg_cap - S
+        soff += [0] * pad
+        slen += [0] * pad
+        spos0 += [0] * pad
+        sdelta += [0] * pad
+        spi += [spi[-1]] * pad
+    if page_cap is not None:
+        if len(pids) > page_cap:
+            raise OverflowError("page capacity")
+        pids += [scratch_page] * (page_cap - len(pids))
+    arrays = {
+        "input_ids": ids, "positions": pos, "slots": slots, "qo_indptr": qo, "seg_indptr": segi,
+        "seg_page_indptr": spi, "seg_offset": soff, "seg_len": slen, "seg_pos0": spos0, "seg_delta": sdelta,
+        "page_ids": pids, "logits_idx": lidx,
+    }
+    arrays = {k: np.asarray(v, dtype=np.int32) for k, v in arrays.items()}
+    sizes = {k: len(v) for k, v in arrays.items()}
+    return Plan(arrays, len(items) + pad_seqs, len(ids), max_q, max_kv,
+                decode=(max_q == 1 and len(ids) == len(items) + pad_seqs), sizes=sizes)
+
+
+def pack(plan: Plan) -> np.ndarray:
+    return np.concatenate([plan.arrays[k] for k in FIELDS])
+
+
+def unpack(buf: torch.Tensor, sizes: dict) -> dict:
+    out, o = {}, 0
+    for k in FIELDS:
+        n = sizes[k]
+        out[k] = buf[o:o + n]
+        o += n
+    return out
+
+
+def make_meta(views: dict, plan: Plan, num_splits: int = 1) -> AttnMeta:
+    host = None
+    if not views["qo_indptr"].is_cuda:
+        host = {k: torch.from_numpy(v) for k, v in plan.arrays.items()}
+    return AttnMeta(qo_indptr=views["qo_indptr"], positions=views["positions"], seg_indptr=views["seg_indptr"],
+                    seg_page_indptr=views["seg_page_indptr"], seg_offset=views["seg_offset"],
+                    seg_len=views["seg_len"], seg_pos0=views["seg_pos0"], seg_delta=views["seg_delta"],
+                    page_ids=views["page_ids"], num_seqs=plan.num_seqs, max_q_len=plan.max_q_len,
+                    max_kv_len=plan.max_kv_len, decode=plan.decode, num_splits=num_splits, host=host)

@@ -1,0 +1,313 @@
+"""Runs the model: builds the per-step plan, executes eager prefill and
+CUDA-graph decode, samples on the device.
+
+Responsibilities of ``braidinfer/engine/model_runner.py:17-307`` (prepare
+inputs, run model, sample, chunk prefill) re-designed for throughput:
+
+* one packed int32 metadata buffer per step (one H2D copy);
+* decode runs as a captured CUDA graph per batch bucket (the reference
+  stored ``enforce_eager`` and never read it); padded rows write to the pool's
+  scratch page;
+* tokens are sampled on the device and read back once per step (the only
+  D2H copy), instead of per-layer ``.item()`` syncs;
+* chunk prefill is a normal batched forward with causal attention restricted
+  to the chunk (the reference returned zeros from chunk prefill,
+  ``braidinfer/layers/attention.py:143-144``).
+"""
+from __future__ import annotations
+
+import time
+from typing import Dict, List, Optional, Tuple
+
+import numpy as np
+import torch
+
+from .. import ops
+from ..config import Config
+from ..models import build_model
+from ..parallel.state import TPState
+from ..utils.logging import get_logger
+from .batch import FwdItem, Plan, build_plan, make_meta, pack, unpack
+from .page_manager import PageManager
+from .sequence import Sequence
+
+log = get_logger("runner")
+
+GRAPH_BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 192, 256)
+
+
+def _num_sms(device) -> int:
+    if device.type == "cuda":
+        return torch.cuda.get_device_properties(device).multi_processor_count
+    return 1
+
+
+class _GraphSlot:
+    def __init__(self):
+        self.graph = None
+        self.meta_buf = None
+        self.sizes = None
+        self.fbuf = None
+        self.ibuf = None
+        self.lbuf = None
+        self.out = None
+        self.hidden = None
+        self.seg_cap = 0
+        self.page_cap = 0
+        self.num_splits = 1
+
+
+class ModelRunner:
+    def __init__(self, config: Config, tp: TPState):
+        self.config = config
+        self.tp = tp
+        self.device = config.torch_device
+        self.dtype = config.torch_dtype
+        spec = config.spec
+        self.spec = spec
+        t0 = time.time()
+        self.model = build_model(spec, tp, self.dtype, self.device, config.max_model_len)
+        if config.load_weights:
+            from ..utils.loader import load_model
+
+            load_model(self.model, config.model)
+        else:
+            self.model.random_init(seed=config.seed, std=config.init_std)
+        log.info("model ready in %.1fs", time.time() - t0)
+        self.page_manager: Optional[PageManager] = None
+        self.page_size = config.kvcache_block_size
+        self.graphs: Dict[int, _GraphSlot] = {}
+        self.sms = _num_sms(self.device)
+        self.timing = {"steps": 0, "prefill_tokens": 0, "decode_tokens": 0}
+        self.capture_logits: Optional[list] = None  # debug/test hook (eager steps only)
+
+    # ------------------------------------------------------------- KV pool
+    def kv_bytes_per_page(self) -> int:
+        L = self.model.layout
+        return 2 * self.spec.num_layers * L.kv_heads * self.page_size * self.spec.head_dim * \
+            torch.tensor([], dtype=self.dtype).element_size()
+
+    def auto_num_pages(self) -> int:
+        cfg = self.config
+        if cfg.num_kvcache_blocks > 0:
+            return cfg.num_kvcache_blocks
+        if self.device.type != "cuda":
+            return 64
+        free, total = torch.cuda.mem_get_info(self.device)
+        used = total - free
+        act = cfg.max_num_batched_tokens * self.spec.hidden_size * 64 + (2 << 30)
+        budget = total * cfg.gpu_memory_utilization - used - act
+        n = int(budget // self.kv_bytes_per_page())
+        if self.tp.size > 1:
+            import torch.distributed as dist
+
+            t = torch.tensor([n], device=self.device)
+            dist.all_reduce(t, op=dist.ReduceOp.MIN, group=self.tp.group)
+            n = int(t.item())
+        return max(n, 16)
+
+    def allocate_kv(self) -> PageManager:
+        L = self.model.layout
+        n = self.auto_num_pages()
+        self.page_manager = PageManager(n, self.page_size, self.spec.num_layers, L.kv_heads, self.spec.head_dim,
+                                        self.dtype, self.device)
+        log.info("KV pool: %d pages x %d tokens (%.2f GB)", n, self.page_size,
+                 n * self.kv_bytes_per_page() / 1e9)
+        return self.page_manager
+
+    # ------------------------------------------------------------ forward
+    def _decode_splits(self, batch: int, max_kv: Optional[int] = None) -> int:
+        L = self.model.layout
+        work = max(1, batch * L.kv_heads)
+        ns = max(1, min(32, -(-2 * self.sms // work)))
+        if max_kv is not None:
+            ns = max(1, min(ns, -(-max_kv // 64)))
+        return ns
+
+    def _upload(self, plan: Plan):
+        host = pack(plan)
+        if self.device.type == "cuda":
+            buf = torch.from_numpy(host).pin_memory().to(self.device, non_blocking=True)
+        else:
+            buf = torch.from_numpy(host)
+        return unpack(buf, plan.sizes)
+
+    def _sampling_tensors(self, seqs: List[Sequence], pad: int = 0):
+        n = len(seqs) + pad
+        f = np.zeros((3, n), dtype=np.float32)
+        k = np.zeros(n, dtype=np.int32)
+        l = np.zeros((2, n), dtype=np.int64)
+        for i, s in enumerate(seqs):
+            f[0, i], f[1, i], f[2, i] = s.temperature, s.top_p, s.min_p
+            k[i] = s.top_k
+            l[0, i], l[1, i] = s.seed, s.num_completion_tokens
+        f[1, len(seqs):] = 1.0
+        return f, k, l
+
+    def _to_dev(self, a: np.ndarray) -> torch.Tensor:
+        t = torch.from_numpy(a)
+        if self.device.type == "cuda":
+            return t.pin_memory().to(self.device, non_blocking=True)
+        return t
+
+    def forward_items(self, items: List[FwdItem]) -> torch.Tensor:
+        """Eager forward; returns final-normed hidden rows of items with ``logits=True``."""
+        plan = build_plan(items, self.page_size)
+        views = self._upload(plan)
+        ns = self._decode_splits(plan.num_seqs, plan.max_kv_len) if plan.decode else 1
+        meta = make_meta(views, plan, ns)
+        kv = self.page_manager.kv_cache
+        h = self.model.forward(views["input_ids"], views["positions"], views["slots"], meta, kv)
+        rows = h.index_select(0, views["logits_idx"].long()) if plan.sizes["logits_idx"] else h[:0]
+        return self.model.final_hidden(rows)
+
+    def _items_for(self, seqs: List[Sequence]) -> List[FwdItem]:
+        items = []
+        for s in seqs:
+            k0 = s.num_cached_tokens
+            toks = s.token_ids[k0:]
+            items.append(FwdItem(tokens=toks, pos0=s.pos_base + k0, priv_index0=k0, priv_pages=s.pages,
+                                 priv_pos0=s.pos_base, segments=s.segments, logits=True))
+        return items
+
+    def sample(self, hn: torch.Tensor, seqs: List[Sequence]) -> torch.Tensor:
+        logits = self.model.compute_logits(hn)
+        if self.capture_logits is not None:
+            self.capture_logits.append(logits.float().cpu())
+        f, k, l = self._sampling_tensors(seqs)
+        ft, kt, lt = self._to_dev(f), self._to_dev(k), self._to_dev(l)
+        return ops.sample(logits, ft[0], kt, ft[1], ft[2], lt[0], lt[1],
+                          all_greedy=all(s.temperature == 0 for s in seqs))
+
+    def run(self, seqs: List[Sequence], is_prefill: bool) -> List[int]:
+        """One engine step for ``seqs``; returns one sampled token per sequence."""
+        self.timing["steps"] += 1
+        if not is_prefill and self.config.use_cuda_graphs and len(seqs) <= self.config.max_graph_batch:
+            out = self._run_graph(seqs)
+            if out is not None:
+                self.timing["decode_tokens"] += len(seqs)
+                return out
+        with_tokens = [s for s in seqs if s.num_tokens > s.num_cached_tokens]
+        rows = []
+        if with_tokens:
+            hn = self.forward_items(self._items_for(with_tokens))
+            rows.append(hn)
+            self.timing["prefill_tokens" if is_prefill else "decode_tokens"] += sum(
+                s.num_tokens - s.num_cached_tokens for s in with_tokens)
+        empty = [s for s in seqs if s.num_tokens <= s.num_cached_tokens]
+        for s in empty:
+            if s.first_hidden is None:
+                raise RuntimeError(f"sequence {s.seq_id} has nothing to process")
+            rows.append(s.first_hidden.to(self.device, self.dtype).view(1, -1))
+        order = with_tokens + empty
+        hn = torch.cat(rows) if len(rows) > 1 else rows[0]
+        toks = self.sample(hn, order).tolist()
+        by_id = {s.seq_id: t for s, t in zip(order, toks)}
+        return [by_id[s.seq_id] for s in seqs]
+
+    def prefill_chunks(self, jobs: List[Tuple[List[int], int, List[int]]]) -> torch.Tensor:
+        """Independent causal prefill of chunks: ``(tokens, cached_pos0, pages)`` each.
+
+        Returns the final-normed hidden state of each chunk's last token.
+        """
+        items = [FwdItem(tokens=t, pos0=p0, priv_index0=0, priv_pages=pg, priv_pos0=p0, segments=[], logits=True)
+                 for t, p0, pg in jobs]
+        budget = self.config.max_num_batched_tokens
+        outs, cur, n = [], [], 0
+        for it in items:
+            if cur and n + len(it.tokens) > budget:
+                outs.append(self.forward_items(cur))
+                cur, n = [], 0
+            cur.append(it)
+            n += len(it.tokens)
+        if cur:
+            outs.append(self.forward_items(cur))
+        self.timing["prefill_tokens"] += sum(len(t) for t, _, _ in jobs)
+        return torch.cat(outs) if len(outs) > 1 else outs[0]
+
+    # --------------------------------------------------------- CUDA graphs
+    def _bucket(self, n: int) -> int:
+        for b in GRAPH_BUCKETS:
+            if b >= n and b <= self.config.max_graph_batch:
+                return b
+        return -1
+
+    def _graph_caps(self, B: int) -> Tuple[int, int]:
+        max_segs = 16
+        pages_per_seq = -(-self.config.max_model_len // self.page_size) + max_segs
+        return B * max_segs, B * pages_per_seq
+
+    def _capture(self, B: int) -> _GraphSlot:
+        g = _GraphSlot()
+        g.seg_cap, g.page_cap = self._graph_caps(B)
+        pm = self.page_manager
+        plan = build_plan([], self.page_size, pad_seqs=B, scratch_page=pm.scratch_page,
+                          seg_cap=g.seg_cap, page_cap=g.page_cap)
+        g.sizes = plan.sizes
+        g.meta_buf = torch.from_numpy(pack(plan)).to(self.device)
+        views = unpack(g.meta_buf, g.sizes)
+        g.num_splits = self._decode_splits(B)
+        meta = make_meta(views, plan, g.num_splits)
+        meta.decode = True
+        meta.max_kv_len = self.config.max_model_len
+        g.fbuf = torch.zeros(3, B, dtype=torch.float32, device=self.device)
+        g.fbuf[1].fill_(1.0)
+        g.ibuf = torch.zeros(B, dtype=torch.int32, device=self.device)
+        g.lbuf = torch.zeros(2, B, dtype=torch.int64, device=self.device)
+        g.out = torch.zeros(B, dtype=torch.int32, device=self.device)
+        kv = pm.kv_cache
+
+        def body():
+            h = self.model.forward(views["input_ids"], views["positions"], views["slots"], meta, kv)
+            hn = self.model.final_hidden(h)
+            logits = self.model.compute_logits(hn)
+            ops.sample(logits, g.fbuf[0], g.ibuf, g.fbuf[1], g.fbuf[2], g.lbuf[0], g.lbuf[1], out=g.out)
+
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                body()
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, pool=self._graph_pool()):
+            body()
+        torch.cuda.synchronize(self.device)
+        g.graph = graph
+        self._pinned_meta = getattr(self, "_pinned_meta", {})
+        return g
+
+    def _graph_pool(self):
+        if not hasattr(self, "_pool"):
+            self._pool = torch.cuda.graph_pool_handle()
+        return self._pool
+
+    def capture_all(self, max_batch: Optional[int] = None) -> None:
+        mb = min(max_batch or self.config.max_graph_batch, self.config.max_graph_batch)
+        for b in sorted(GRAPH_BUCKETS, reverse=True):
+            if b <= mb and b not in self.graphs:
+                self.graphs[b] = self._capture(b)
+
+    def _run_graph(self, seqs: List[Sequence]) -> Optional[List[int]]:
+        B = self._bucket(len(seqs))
+        if B < 0:
+            return None
+        g = self.graphs.get(B)
+        if g is None:
+            g = self.graphs[B] = self._capture(B)
+        try:
+            plan = build_plan(self._items_for(seqs), self.page_size, pad_seqs=B - len(seqs),
+                              scratch_page=self.page_manager.scratch_page, seg_cap=g.seg_cap, page_cap=g.page_cap)
+        except OverflowError:
+            return None
+        if plan.sizes != g.sizes:
+            return None
+        host = torch.from_numpy(pack(plan)).pin_memory()
+        g.meta_buf.copy_(host, non_blocking=True)
+        f, k, l = self._sampling_tensors(seqs, pad=B - len(seqs))
+        g.fbuf.copy_(torch.from_numpy(f).pin_memory(), non_blocking=True)
+        g.ibuf.copy_(torch.from_numpy(k).pin_memory(), non_blocking=True)
+        g.lbuf.copy_(torch.from_numpy(l).pin_memory(), non_blocking=True)
+        g.graph.replay()
+        return g.out[: len(seqs)].tolist()

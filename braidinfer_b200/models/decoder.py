@@ -1,0 +1,245 @@
+"""Llama-style decoder (Llama / TinyLlama / Llama-3, Qwen3, ERNIE-4.5).
+
+One implementation serves the reference's three RMSNorm/SwiGLU/RoPE model
+files (``braidinfer/models/llama.py``, ``qwen3.py``, ``ernie.py``); the
+differences are data: Qwen3's per-head ``q_norm``/``k_norm``, optional QKV
+bias, tied embeddings, and ERNIE's interleaved ("GLM") rotary pairs, which
+are turned into the neox half-split convention by permuting each head's q/k
+projection rows at load time (a permutation applied to both q and k leaves
+q·k unchanged).
+
+HF semantics are kept where the reference deviated: no ``1/sqrt(hidden)``
+embedding scaling for Qwen3 (``braidinfer/models/qwen3.py:465``), ``lm_head``
+tied to ``embed_tokens`` when ``tie_word_embeddings`` is set, K cached after
+k_norm and RoPE and never re-normalised at attention time.
+
+Per layer the forward runs: RMSNorm → QKV GEMM (+bias) → fused q/k-norm +
+RoPE(k) + paged KV append → cascade attention (query-side differential RoPE)
+→ o_proj GEMM with the residual add in its epilogue (or the TP reduction) →
+RMSNorm → gate/up GEMM with SwiGLU in its epilogue → down GEMM + residual.
+"""
+from __future__ import annotations
+
+import math
+from typing import Dict, Optional
+
+import torch
+
+from .. import ops
+from ..config import ModelSpec
+from ..parallel import comm
+from ..parallel.layout import TPLayout
+from ..parallel.state import TPState
+
+
+class LayerWeights:
+    __slots__ = ("in_norm", "qkv_w", "qkv_b", "q_norm", "k_norm", "o_w", "o_b", "post_norm", "gu_w",
+                 "down_w", "in_norm_b", "post_norm_b", "fc_b", "down_b")
+
+    def __init__(self):
+        for s in self.__slots__:
+            setattr(self, s, None)
+
+
+class DecoderLM:
+    packed_modules_mapping = {
+        "q_proj": ("qkv_proj", "q"),
+        "k_proj": ("qkv_proj", "k"),
+        "v_proj": ("qkv_proj", "v"),
+        "gate_proj": ("gate_up_proj", 0),
+        "up_proj": ("gate_up_proj", 1),
+    }
+
+    def __init__(self, spec: ModelSpec, tp: TPState, dtype: torch.dtype, device: torch.device,
+                 max_pos: int):
+        self.spec = spec
+        self.tp = tp
+        self.dtype = dtype
+        self.device = device
+        self.layout = TPLayout(tp.size, tp.rank, spec.num_heads, spec.num_kv_heads, spec.head_dim,
+                               spec.intermediate_size, spec.vocab_size)
+        L = self.layout
+        D = spec.head_dim
+        H = spec.hidden_size
+        kw = dict(dtype=dtype, device=device)
+        self.qkv_rows = (L.q_heads + 2 * L.kv_heads) * D
+        self.layers = []
+        for _ in range(spec.num_layers):
+            w = LayerWeights()
+            w.in_norm = torch.ones(H, **kw)
+            w.qkv_w = torch.empty(self.qkv_rows, H, **kw)
+            if spec.attention_bias:
+                w.qkv_b = torch.zeros(self.qkv_rows, **kw)
+            if spec.qk_norm:
+                w.q_norm = torch.ones(D, **kw)
+                w.k_norm = torch.ones(D, **kw)
+            w.o_w = torch.empty(H, L.q_heads * D, **kw)
+            w.post_norm = torch.ones(H, **kw)
+            w.gu_w = torch.zeros(2 * L.inter_pad, H, **kw)
+            w.down_w = torch.zeros(H, L.inter_pad, **kw)
+            self.layers.append(w)
+        self.embed = torch.empty(L.vocab_local, H, **kw)
+        self.final_norm = torch.ones(H, **kw)
+        self.lm_head = self.embed if spec.tie_word_embeddings else torch.empty(L.vocab_local, H, **kw)
+        # RoPE tables: room for query positions shifted by chunk deltas.
+        self.rope_len = 2 * max_pos + 16
+        if spec.use_rope:
+            self.cos, self.sin = ops.build_cos_sin(D, spec.rope_theta, self.rope_len, spec.rope_scaling, device)
+        else:
+            self.cos = self.sin = torch.zeros(1, max(1, D // 2), device=device)
+        self.scale = 1.0 / math.sqrt(D)
+        # ERNIE: interleaved rotary pairs -> neox half split by a row permutation.
+        self.rope_perm = None
+        if spec.family == "ernie":
+            self.rope_perm = torch.cat([torch.arange(0, D, 2), torch.arange(1, D, 2)])
+
+    # ------------------------------------------------------------------ init
+    def random_init(self, seed: int = 0, std: float = 0.02, k_norm_range: Optional[float] = None) -> None:
+        g = torch.Generator(device=self.device)
+        g.manual_seed(seed + 7919 * self.tp.rank)
+
+        def fill(t):
+            t.normal_(0.0, std, generator=g)
+
+        L = self.layout
+        for w in self.layers:
+            fill(w.qkv_w)
+            fill(w.o_w)
+            gu = w.gu_w.view(-1, 2 * L.block, w.gu_w.shape[1])
+            # only the unpadded intermediate rows carry weights
+            n_blocks = -(-L.inter // L.block)
+            fill(gu[:n_blocks])
+            if L.inter % L.block:
+                tail = L.inter % L.block
+                gu[n_blocks - 1, tail:L.block].zero_()
+                gu[n_blocks - 1, L.block + tail:].zero_()
+            fill(w.down_w[:, :L.inter])
+            if k_norm_range is not None and w.k_norm is not None:
+                w.k_norm.uniform_(-k_norm_range, k_norm_range, generator=g)
+        fill(self.embed)
+        if self.lm_head is not self.embed:
+            fill(self.lm_head)
+
+    # --------------------------------------------------------------- loading
+    def load_hf_tensor(self, name: str, t: torch.Tensor) -> bool:
+        """Copy one HF checkpoint tensor (full, unsharded) into this rank's shard."""
+        L, S = self.layout, self.spec
+        D = S.head_dim
+        t = t.to(self.dtype)
+        if name in ("model.embed_tokens.weight", "embed_tokens.weight"):
+            self.embed.copy_(t[L.vocab_start:L.vocab_start + L.vocab_local])
+            return True
+        if name in ("lm_head.weight",):
+            if self.lm_head is self.embed:
+                return True
+            self.lm_head.copy_(t[L.vocab_start:L.vocab_start + L.vocab_local])
+            return True
+        if name in ("model.norm.weight", "norm.weight"):
+            self.final_norm.copy_(t)
+            return True
+        if not name.startswith("model.layers."):
+            return False
+        parts = name.split(".")
+        li = int(parts[2])
+        w = self.layers[li]
+        sub = ".".join(parts[3:])
+        qh0, qh = L.q_head_start, L.q_heads
+        kh0, kh = L.kv_head_start, L.kv_heads
+        q_rows, kv_rows = qh * D, kh * D
+
+        def head_rows(x, h0, nh, permute):
+            x = x.view(-1, D, *x.shape[1:])[h0:h0 + nh]
+            if permute and self.rope_perm is not None:
+                x = x[:, self.rope_perm.to(x.device)]
+            return x.reshape(nh * D, *x.shape[2:])
+
+        if sub == "input_layernorm.weight":
+            w.in_norm.copy_(t)
+        elif sub == "post_attention_layernorm.weight":
+            w.post_norm.copy_(t)
+        elif sub in ("self_attn.q_proj.weight", "self_attn.q_proj.bias"):
+            dst = w.qkv_w if sub.endswith("weight") else w.qkv_b
+            if dst is None:
+                return True
+            dst[:q_rows].copy_(head_rows(t, qh0, qh, True))
+        elif sub in ("self_attn.k_proj.weight", "self_attn.k_proj.bias"):
+            dst = w.qkv_w if sub.endswith("weight") else w.qkv_b
+            if dst is None:
+                return True
+            dst[q_rows:q_rows + kv_rows].copy_(head_rows(t, kh0, kh, True))
+        elif sub in ("self_attn.v_proj.weight", "self_attn.v_proj.bias"):
+            dst = w.qkv_w if sub.endswith("weight") else w.qkv_b
+            if dst is None:
+                return True
+            dst[q_rows + kv_rows:q_rows + 2 * kv_rows].copy_(head_rows(t, kh0, kh, False))
+        elif sub == "self_attn.q_norm.weight":
+            if w.q_norm is not None:
+                w.q_norm.copy_(t)
+        elif sub == "self_attn.k_norm.weight":
+            if w.k_norm is not None:
+                w.k_norm.copy_(t)
+        elif sub == "self_attn.o_proj.weight":
+            w.o_w.copy_(t[:, qh0 * D:(qh0 + qh) * D])
+        elif sub in ("mlp.gate_proj.weight", "mlp.up_proj.weight"):
+            rows = t[L.inter_start:L.inter_start + L.inter]
+            gu = w.gu_w.view(-1, 2, L.block, t.shape[1])
+            half = 0 if "gate" in sub else 1
+            flat = gu[:, half].reshape(-1, t.shape[1])
+            flat[:L.inter].copy_(rows)
+            gu[:, half].copy_(flat.view(-1, L.block, t.shape[1]))
+        elif sub == "mlp.down_proj.weight":
+            w.down_w[:, :L.inter].copy_(t[:, L.inter_start:L.inter_start + L.inter])
+        elif sub.endswith("rotary_emb.inv_freq"):
+            pass
+        else:
+            return False
+        return True
+
+    # --------------------------------------------------------------- forward
+    def embed_tokens(self, input_ids: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
+        h = ops.embedding(input_ids, self.embed, self.layout.vocab_start)
+        if self.tp.size > 1:
+            h = comm.all_reduce(h)
+        return h
+
+    def forward(self, input_ids: torch.Tensor, positions: torch.Tensor, slot_mapping: torch.Tensor,
+                meta, kv_cache: torch.Tensor, workspace: Optional[Dict] = None) -> torch.Tensor:
+        """Return the residual stream ``[T, hidden]`` after the last layer (pre final norm)."""
+        S, L = self.spec, self.layout
+        residual = self.embed_tokens(input_ids, positions)
+        x = ops.rms_norm(residual, self.layers[0].in_norm, S.rms_norm_eps)
+        n = len(self.layers)
+        for i, w in enumerate(self.layers):
+            qkv = ops.linear(x, w.qkv_w, w.qkv_b)
+            q = ops.qkv_prepare(qkv, positions, slot_mapping, kv_cache[i], L.q_heads, L.kv_heads, S.head_dim,
+                                self.cos, self.sin, w.q_norm, w.k_norm, S.rms_norm_eps, S.use_rope)
+            o = ops.attention(q, kv_cache[i], meta, self.cos, self.sin, self.scale, S.use_rope, workspace)
+            if self.tp.size == 1:
+                residual = ops.linear(o, w.o_w, residual=residual)
+                x = ops.rms_norm(residual, w.post_norm, S.rms_norm_eps)
+            else:
+                x, residual = comm.all_reduce_add_rms_norm(ops.linear(o, w.o_w), residual, w.post_norm,
+                                                           S.rms_norm_eps)
+            g = ops.linear_swiglu(x, w.gu_w)
+            nxt = self.layers[i + 1].in_norm if i + 1 < n else None
+            if self.tp.size == 1:
+                residual = ops.linear(g, w.down_w, residual=residual)
+                if nxt is not None:
+                    x = ops.rms_norm(residual, nxt, S.rms_norm_eps)
+            else:
+                if nxt is not None:
+                    x, residual = comm.all_reduce_add_rms_norm(ops.linear(g, w.down_w), residual, nxt,
+                                                               S.rms_norm_eps)
+                else:
+                    residual = residual + comm.all_reduce(ops.linear(g, w.down_w))
+        return residual
+
+    def final_hidden(self, h: torch.Tensor) -> torch.Tensor:
+        return ops.rms_norm(h, self.final_norm, self.spec.rms_norm_eps)
+
+    def compute_logits(self, hn: torch.Tensor) -> torch.Tensor:
+        """Full-vocabulary logits ``[B, V]`` from final-normed rows ``hn``."""
+        local = ops.linear(hn, self.lm_head)
+        if self.tp.size > 1:
+            return comm.all_gather_last(local, self.spec.vocab_size)
+        return local

@@ -1,0 +1,36 @@
+"""Loader of the in-tree native extension ``braidinfer_b200._C``.
+
+The extension holds every hand-written sm_100a kernel.  CUDA tensors must go
+through it: if it is missing on a GPU box the op raises
+``KernelUnavailableError`` instead of silently falling back to PyTorch.  CPU
+tensors use the PyTorch restatement of each op, which is the numerical oracle
+of the tests (and the only way the engine runs without a GPU).
+"""
+from __future__ import annotations
+
+from ..errors import KernelUnavailableError
+
+_C = None
+_err: Exception | None = None
+
+
+def ext():
+    global _C, _err
+    if _C is None:
+        try:
+            from .. import _C as mod  # type: ignore[attr-defined]
+        except Exception as e:  # pragma: no cover - depends on build
+            _err = e
+            raise KernelUnavailableError(
+                "braidinfer_b200._C is not built; run `python setup.py build_ext --inplace` "
+                f"(import error: {e})") from e
+        _C = mod
+    return _C
+
+
+def available() -> bool:
+    try:
+        ext()
+        return True
+    except KernelUnavailableError:
+        return False

@@ -1,0 +1,93 @@
+"""GEMM entry points: ``y = x @ w.T`` with fused epilogues.
+
+On CUDA these run the hand-written tcgen05 kernel (``csrc/gemm_tcgen05.cu``):
+TMA-fed shared-memory stages, one elected thread issuing ``tcgen05.mma`` into a
+TMEM accumulator, and an epilogue warp group that adds bias/residual or
+applies SwiGLU before the bf16 store.  Decode-sized ``M`` swaps operands so the
+weight rows fill the 128-wide MMA M dimension.
+
+Epilogue rounding mirrors an HF forward: the GEMM result is rounded to bf16
+before the residual add, and SwiGLU rounds gate, up and ``silu(gate)`` to
+bf16 before the product (``braidinfer/layers/activation.py:6-13``).
+
+SwiGLU weights are stored block-interleaved: rows ``[g0..g63, u0..u63, g64..]``
+(blocks of ``SWIGLU_BLOCK``) so one 128-row tile holds matching gate and up
+rows.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.nn.functional as F
+
+from ._ext import ext
+
+SWIGLU_BLOCK = 64
+
+
+def _round(t: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    return t.to(dtype).float() if dtype != torch.float32 else t
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None,
+           residual: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if x.is_cuda:
+        M = x.shape[0]
+        out = torch.empty(M, w.shape[0], dtype=x.dtype, device=x.device) if out is None else out
+        ext().gemm(out, x, w, bias, residual, 0)
+        return out
+    y = F.linear(x.float(), w.float(), None if bias is None else bias.float())
+    if residual is not None:
+        y = _round(y, x.dtype) + residual.float()
+    y = y.to(x.dtype)
+    if out is not None:
+        out.copy_(y)
+        return out
+    return y
+
+
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor, block: int = SWIGLU_BLOCK) -> torch.Tensor:
+    """``[I, K] x2 -> [2*I_pad, K]`` with zero-padded ``I_pad = ceil(I/block)*block``."""
+    I, K = gate.shape
+    Ip = (I + block - 1) // block * block
+    if Ip != I:
+        z = gate.new_zeros(Ip - I, K)
+        gate, up = torch.cat([gate, z]), torch.cat([up, z])
+    g = gate.view(Ip // block, block, K)
+    u = up.view(Ip // block, block, K)
+    return torch.stack([g, u], dim=1).reshape(2 * Ip, K).contiguous()
+
+
+def swiglu_ref_from_interleaved(y: torch.Tensor, dtype: torch.dtype, block: int = SWIGLU_BLOCK) -> torch.Tensor:
+    M, N2 = y.shape
+    y = y.view(M, N2 // (2 * block), 2, block)
+    g = _round(y[:, :, 0], dtype)
+    u = _round(y[:, :, 1], dtype)
+    s = _round(F.silu(g), dtype)
+    return (s * u).reshape(M, N2 // 2).to(dtype)
+
+
+def linear_swiglu(x: torch.Tensor, w_gu: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``silu(x @ Wg.T) * (x @ Wu.T)`` from the block-interleaved ``w_gu``."""
+    if x.is_cuda:
+        M = x.shape[0]
+        out = torch.empty(M, w_gu.shape[0] // 2, dtype=x.dtype, device=x.device) if out is None else out
+        ext().gemm(out, x, w_gu, None, None, 1)
+        return out
+    y = F.linear(x.float(), w_gu.float())
+    r = swiglu_ref_from_interleaved(y, x.dtype)
+    if out is not None:
+        out.copy_(r)
+        return out
+    return r
+
+
+def gelu_new(x: torch.Tensor) -> torch.Tensor:
+    """GPT-2's tanh GELU (``braidinfer/layers/activation.py:16-25``)."""
+    if x.is_cuda:
+        out = torch.empty_like(x)
+        ext().gelu_tanh(out, x)
+        return out
+    xf = x.float()
+    return (0.5 * xf * (1.0 + torch.tanh(0.7978845608028654 * (xf + 0.044715 * xf.pow(3))))).to(x.dtype)

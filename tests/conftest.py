@@ -1,0 +1,31 @@
+import os
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200, sm_100a) and the built extension")
+    config.addinivalue_line("markers", "multigpu: needs 2+ GPUs")
+
+
+def pytest_collection_modifyitems(config, items):
+    import torch
+
+    if torch.cuda.is_available():
+        return
+    skip = pytest.mark.skip(reason="no CUDA device")
+    for it in items:
+        if "gpu" in it.keywords:
+            it.add_marker(skip)
+
+
+@pytest.fixture(scope="session")
+def tiny_llama_dir(tmp_path_factory):
+    from braidinfer_b200.utils.synthetic import make_checkpoint
+
+    return make_checkpoint(str(tmp_path_factory.mktemp("tiny_llama")), "tiny-llama", seed=0, dtype=__import__("torch").float32)
