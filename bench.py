@@ -1,0 +1,275 @@
+"""Headline benchmark: batched greedy decode throughput (tokens/s) of a
+Llama-3-8B-architecture model (random-init bf16 weights, synthetic prompts),
+tensor-parallel over the GPUs of one node.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--prompt-len S]
+    torchrun --nproc-per-node N bench.py --gpus N ...        (N > 1)
+    python bench.py --impl reference ...                     (the reference build)
+
+Timing: W untimed decode steps, then K timed decode steps bracketed by a
+barrier and ``torch.cuda.synchronize()``.  ``value`` is device time: CUDA
+events around each step's graph replay, summed, max over ranks.  ``e2e`` is
+the same K steps timed on the host through the public engine API
+(``LLM.step``), which includes each step's host->device metadata upload from
+pinned memory and the device->host read of the sampled tokens.  Weights
+(16 GB) exceed L2 (126 MB) so no flush is needed between steps.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+
+PUBLISHED_BS8 = 237.0  # reference README.md:68, RTX 4090 / TinyLlama (other hardware & model)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=16)
+    ap.add_argument("--batch", type=int, default=8)
+    ap.add_argument("--prompt-len", type=int, default=2048)
+    ap.add_argument("--model", default="llama3-8b")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--comm", default="fused", choices=["fused", "nccl"])
+    return ap.parse_args()
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.idx = device_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        if not self.path or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.path)
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def make_config_dir(preset: str, with_weights: bool, rank: int = 0) -> str:
+    from braidinfer_b200.utils.synthetic import make_checkpoint
+
+    d = os.path.join(tempfile.gettempdir(), f"braid_bench_{preset}_{'w' if with_weights else 'cfg'}")
+    if rank == 0 and not os.path.exists(os.path.join(d, "config.json" if not with_weights else "model.safetensors")):
+        make_checkpoint(d, preset, write_weights=with_weights)
+    return d
+
+
+def prompts_for(batch: int, plen: int, vocab: int, seed: int = 3):
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
+    return [torch.randint(3, vocab, (plen,), generator=g).tolist() for _ in range(batch)]
+
+
+# --------------------------------------------------------------------- ours
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, ROOT)
+    from braidinfer_b200 import LLM, SamplingParams
+    from braidinfer_b200.ops import _ext
+
+    n = args.gpus
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if n > 1 and not dist.is_initialized():
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    cfg_dir = make_config_dir(args.model, with_weights=False, rank=rank)
+    if n > 1:
+        dist.barrier()
+    max_len = args.prompt_len + args.warmup + args.steps + 64
+    page = 256
+    pages = args.batch * (-(-max_len // page)) + 8
+    llm = LLM(cfg_dir, load_weights=False, tensor_parallel_size=n, max_num_seqs=args.batch,
+              max_model_len=max_len, num_kvcache_blocks=pages, kvcache_block_size=page,
+              max_graph_batch=max(args.batch, 1), comm_backend=args.comm, max_num_batched_tokens=max(16384, max_len))
+    vocab = llm.config.spec.vocab_size
+    sp = SamplingParams(temperature=0.0, max_tokens=args.warmup + args.steps + 4, ignore_eos=True)
+    for p in prompts_for(args.batch, args.prompt_len, vocab):
+        llm.add_request(p, sp)
+    # prefill
+    while llm.scheduler.waiting:
+        llm.step()
+    runner = llm.model_runner
+    for _ in range(args.warmup):
+        llm.step()
+    # count our kernel launches of one decode step (graph contents)
+    launches = runner.launches_per_decode_step(args.batch)
+    torch.cuda.synchronize()
+    if n > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    runner.event_log = []
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            llm.step()
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+    if n > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    dev_ms = sum(a.elapsed_time(b) for a, b in runner.event_log)
+    runner.event_log = None
+    if len(llm.scheduler.running) != args.batch:
+        raise RuntimeError("batch shrank during the timed region")
+    t = torch.tensor([dev_ms, wall], device="cuda", dtype=torch.float64)
+    if n > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dev_ms, wall = float(t[0]), float(t[1])
+    toks = args.batch * args.steps
+    value = toks / (dev_ms / 1e3)
+    e2e = toks / wall
+    if rank == 0:
+        B = args.batch
+        plan_bytes = runner.last_h2d_bytes
+        line = {
+            "metric": f"decode tok/s (bs{B}) {args.model} TP{n}",
+            "value": round(value, 2), "unit": "tokens/s", "n_gpus": n, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(dev_ms / args.steps, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": round(value / PUBLISHED_BS8, 3) if B == 8 else None,
+            "dtype": "bf16", "data": "synthetic token ids (seed 3), random-init N(0,0.02) weights",
+            "config": {"model": args.model, "global_batch": B, "seq_len": args.prompt_len,
+                       "parallelism": f"tp{n}", "l2": "weights (16 GB) larger than L2; no flush",
+                       "decode": "CUDA-graph step, greedy, paged HND KV (page 256)", "comm": args.comm if n > 1 else None},
+            "clocks": clocks.summary(),
+            "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": plan_bytes,
+                    "d2h_bytes_per_step": 4 * B, "api": "LLM.add_request + LLM.step"},
+            "gpu_launches": launches * args.steps,
+            "gpu_launches_per_step": launches,
+            "impl": "ours",
+        }
+        print(json.dumps(line), flush=True)
+    llm.exit()
+    if n > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------- reference
+def run_reference(args) -> None:
+    n = args.gpus
+    rank = int(os.environ.get("RANK", "0"))
+    if n > 1:
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable":
+                              "the reference is single-GPU: no live tensor-parallel path (its only collective is "
+                              "dead code in braidinfer/layers/linear_distributed.py)"}), flush=True)
+        return
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "braidinfer")):
+        print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref not installed"}), flush=True)
+        return
+    sys.path.insert(0, ref)
+    import torch
+
+    d = make_config_dir(args.model, with_weights=True)
+    from braidinfer import LLM, SamplingParams  # the unmodified reference
+
+    # The reference raises NotImplementedError for batch > 1
+    # (braidinfer/layers/attention.py:146-147), so the batch's requests run one
+    # after another through its public generate(stream=True) API.
+    llm = LLM(d, num_kvcache_blocks=-(-(args.prompt_len + args.warmup + args.steps + 64) // 256) + 4,
+              max_model_len=args.prompt_len + args.warmup + args.steps + 64)
+    prompts = prompts_for(args.batch, args.prompt_len, llm.config.hf_config.vocab_size)
+    sp = SamplingParams(temperature=0.0, max_tokens=args.warmup + args.steps + 1, ignore_eos=True)
+    import contextlib
+    import io
+
+    dev_ms, wall, toks = 0.0, 0.0, 0
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        for p in prompts:
+            evs, times = [], []
+            with contextlib.redirect_stdout(io.StringIO()):
+                for item in llm.generate(p, sp, stream=True):
+                    e = torch.cuda.Event(enable_timing=True)
+                    e.record()
+                    evs.append(e)
+                    times.append(time.perf_counter())
+            torch.cuda.synchronize()
+            # token records: 0..warmup-1 untimed; then `steps` timed intervals
+            a, b = args.warmup, args.warmup + args.steps
+            if len(evs) <= b:
+                raise RuntimeError("reference produced fewer tokens than requested")
+            dev_ms += evs[a].elapsed_time(evs[b])
+            wall += times[b] - times[a]
+            toks += args.steps
+    value = toks / (dev_ms / 1e3)
+    print(json.dumps({
+        "metric": f"decode tok/s (bs{args.batch}) {args.model} TP1", "value": round(value, 2), "unit": "tokens/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dev_ms / args.steps / args.batch, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": round(value / PUBLISHED_BS8, 3), "dtype": "bf16",
+        "data": "synthetic token ids (seed 3), random-init N(0,0.02) weights",
+        "config": {"model": args.model, "global_batch": args.batch, "seq_len": args.prompt_len, "parallelism": "tp1",
+                   "note": "reference cannot batch: requests decoded one at a time (lower bound)"},
+        "clocks": clocks.summary(), "e2e": {"value": round(toks / wall, 2), "unit": "tokens/s",
+                                            "h2d_bytes_per_step": None, "d2h_bytes_per_step": None},
+        "impl": "reference"}), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -55,6 +55,8 @@ class _GraphSlot:
         self.seg_cap = 0
         self.page_cap = 0
         self.num_splits = 1
+        self.launches = 0
+        self.pin_meta = self.pin_f = self.pin_k = self.pin_l = self.pin_out = None
 
 
 class ModelRunner:
@@ -80,6 +82,8 @@ class ModelRunner:
         self.sms = _num_sms(self.device)
         self.timing = {"steps": 0, "prefill_tokens": 0, "decode_tokens": 0}
         self.capture_logits: Optional[list] = None  # debug/test hook (eager steps only)
+        self.event_log: Optional[list] = None  # (start, end) CUDA events around each graph replay
+        self.last_h2d_bytes = 0
 
     # ------------------------------------------------------------- KV pool
     def kv_bytes_per_page(self) -> int:
@@ -271,8 +275,12 @@ class ModelRunner:
         torch.cuda.current_stream(self.device).wait_stream(s)
         torch.cuda.synchronize(self.device)
         graph = torch.cuda.CUDAGraph()
+        from ..ops import _ext
+
+        n0 = _ext.launches
         with torch.cuda.graph(graph, pool=self._graph_pool()):
             body()
+        g.launches = _ext.launches - n0
         torch.cuda.synchronize(self.device)
         g.graph = graph
         self._pinned_meta = getattr(self, "_pinned_meta", {})
@@ -303,11 +311,37 @@ class ModelRunner:
             return None
         if plan.sizes != g.sizes:
             return None
-        host = torch.from_numpy(pack(plan)).pin_memory()
-        g.meta_buf.copy_(host, non_blocking=True)
+        # Persistent pinned staging: the previous step's copies completed at its
+        # token read-back, so the buffers are free to overwrite.
+        if g.pin_meta is None:
+            g.pin_meta = torch.empty(g.meta_buf.numel(), dtype=torch.int32).pin_memory()
+            g.pin_f = torch.empty(3, B, dtype=torch.float32).pin_memory()
+            g.pin_k = torch.empty(B, dtype=torch.int32).pin_memory()
+            g.pin_l = torch.empty(2, B, dtype=torch.int64).pin_memory()
+            g.pin_out = torch.empty(B, dtype=torch.int32).pin_memory()
+        packed = pack(plan)
+        g.pin_meta.numpy()[:] = packed
         f, k, l = self._sampling_tensors(seqs, pad=B - len(seqs))
-        g.fbuf.copy_(torch.from_numpy(f).pin_memory(), non_blocking=True)
-        g.ibuf.copy_(torch.from_numpy(k).pin_memory(), non_blocking=True)
-        g.lbuf.copy_(torch.from_numpy(l).pin_memory(), non_blocking=True)
-        g.graph.replay()
-        return g.out[: len(seqs)].tolist()
+        g.pin_f.numpy()[:] = f
+        g.pin_k.numpy()[:] = k
+        g.pin_l.numpy()[:] = l
+        g.meta_buf.copy_(g.pin_meta, non_blocking=True)
+        g.fbuf.copy_(g.pin_f, non_blocking=True)
+        g.ibuf.copy_(g.pin_k, non_blocking=True)
+        g.lbuf.copy_(g.pin_l, non_blocking=True)
+        self.last_h2d_bytes = packed.nbytes + f.nbytes + k.nbytes + l.nbytes
+        if self.event_log is not None:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            g.graph.replay()
+            e1.record()
+            self.event_log.append((e0, e1))
+        else:
+            g.graph.replay()
+        g.pin_out.copy_(g.out, non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        return g.pin_out[: len(seqs)].tolist()
+
+    def launches_per_decode_step(self, batch: int) -> int:
+        g = self.graphs.get(self._bucket(batch))
+        return getattr(g, "launches", 0) if g is not None else 0

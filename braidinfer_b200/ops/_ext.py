@@ -13,6 +13,32 @@ from ..errors import KernelUnavailableError
 _C = None
 _err: Exception | None = None
 
+# Number of native kernel launches issued through ``ext()`` (each binding
+# launches one kernel; ops that launch more add the difference via ``count``).
+launches = 0
+
+
+class _Counted:
+    def __init__(self, mod):
+        self._mod = mod
+
+    def __getattr__(self, name):
+        fn = getattr(self._mod, name)
+        if not callable(fn):
+            return fn
+
+        def call(*a, **kw):
+            global launches
+            launches += 1
+            return fn(*a, **kw)
+
+        return call
+
+
+def count(n: int) -> None:
+    global launches
+    launches += n
+
 
 def ext():
     global _C, _err
@@ -24,7 +50,7 @@ def ext():
             raise KernelUnavailableError(
                 "braidinfer_b200._C is not built; run `python setup.py build_ext --inplace` "
                 f"(import error: {e})") from e
-        _C = mod
+        _C = _Counted(mod)
     return _C
 
 

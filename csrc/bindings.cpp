@@ -1,0 +1,39 @@
+// Python bindings of the native sm_100a kernels (module braidinfer_b200._C).
+#include <torch/extension.h>
+
+namespace braid {
+void gemm(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
+          c10::optional<torch::Tensor> residual, int64_t epi);
+int64_t gemm_check_error(int64_t device);
+void attention(torch::Tensor out, torch::Tensor q, torch::Tensor kv, torch::Tensor qo_indptr,
+               torch::Tensor positions, torch::Tensor seg_indptr, torch::Tensor seg_page_indptr,
+               torch::Tensor seg_offset, torch::Tensor seg_len, torch::Tensor seg_pos0, torch::Tensor seg_delta,
+               torch::Tensor page_ids, torch::Tensor cos, torch::Tensor sin, double scale, bool use_rope,
+               int64_t num_seqs, int64_t max_q_len, int64_t max_kv_len, bool decode, int64_t num_splits,
+               c10::optional<torch::Tensor> part_o, c10::optional<torch::Tensor> part_lse);
+void rms_norm(torch::Tensor out, torch::Tensor x, torch::Tensor w, double eps);
+void add_rms_norm(torch::Tensor out, torch::Tensor residual, torch::Tensor x, torch::Tensor w, double eps);
+void layer_norm(torch::Tensor out, torch::Tensor x, torch::Tensor w, torch::Tensor b, double eps);
+void gelu_tanh(torch::Tensor out, torch::Tensor x);
+void embedding(torch::Tensor out, torch::Tensor ids, torch::Tensor w, int64_t vocab_start);
+void qkv_prepare(torch::Tensor q_out, torch::Tensor qkv, torch::Tensor positions, torch::Tensor slots,
+                 torch::Tensor kv, c10::optional<torch::Tensor> q_norm, c10::optional<torch::Tensor> k_norm,
+                 double eps, torch::Tensor cos, torch::Tensor sin, int64_t Hq, int64_t Hkv, int64_t D,
+                 bool use_rope);
+void sample(torch::Tensor out, torch::Tensor logits, torch::Tensor temperature, torch::Tensor top_k,
+            torch::Tensor top_p, torch::Tensor min_p, torch::Tensor seed, torch::Tensor step, bool all_greedy);
+}  // namespace braid
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "braidinfer_b200 native sm_100a kernels";
+  m.def("gemm", &braid::gemm, "tcgen05 GEMM out = x @ w^T (+bias)(+residual); epi 1 = SwiGLU");
+  m.def("gemm_check_error", &braid::gemm_check_error, "read and clear the GEMM bounded-wait error flag");
+  m.def("attention", &braid::attention, "paged cascade attention (decode/prefill)");
+  m.def("rms_norm", &braid::rms_norm);
+  m.def("add_rms_norm", &braid::add_rms_norm);
+  m.def("layer_norm", &braid::layer_norm);
+  m.def("gelu_tanh", &braid::gelu_tanh);
+  m.def("embedding", &braid::embedding);
+  m.def("qkv_prepare", &braid::qkv_prepare);
+  m.def("sample", &braid::sample);
+}

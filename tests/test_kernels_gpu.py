@@ -1,0 +1,193 @@
+"""Numerics of the native sm_100a kernels against fp32 PyTorch references."""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _ext():
+    from braidinfer_b200.ops._ext import ext
+    return ext()
+
+
+def _check_err():
+    assert _ext().gemm_check_error(torch.cuda.current_device()) == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 256, 512), (7, 4096, 1024), (16, 1536, 2048), (33, 640, 256),
+                                   (64, 2048, 4096), (65, 384, 512), (200, 1024, 1024), (1000, 2560, 2048),
+                                   (513, 6144, 4096)])
+def test_gemm_plain(M, N, K):
+    g = torch.Generator(device=DEV).manual_seed(M * 7 + N)
+    x = torch.randn(M, K, device=DEV, generator=g).bfloat16()
+    w = (torch.randn(N, K, device=DEV, generator=g) * 0.05).bfloat16()
+    out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    _ext().gemm(out, x, w, None, None, 0)
+    torch.cuda.synchronize()
+    _check_err()
+    ref = x.float() @ w.float().t()
+    torch.testing.assert_close(out.float(), ref, atol=2e-2 * math.sqrt(K / 256), rtol=2e-2)
+
+
+@pytest.mark.parametrize("M,N,K", [(3, 512, 1024), (100, 768, 512)])
+def test_gemm_bias_residual(M, N, K):
+    x = torch.randn(M, K, device=DEV).bfloat16()
+    w = (torch.randn(N, K, device=DEV) * 0.05).bfloat16()
+    b = torch.randn(N, device=DEV).bfloat16()
+    r = torch.randn(M, N, device=DEV).bfloat16()
+    out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    _ext().gemm(out, x, w, b, r, 0)
+    ref = (x.float() @ w.float().t() + b.float()).bfloat16().float() + r.float()
+    torch.testing.assert_close(out.float(), ref, atol=5e-2, rtol=2e-2)
+    # in place residual update (out aliases the residual)
+    r2 = r.clone()
+    _ext().gemm(r2, x, w, b, r2, 0)
+    torch.testing.assert_close(r2.float(), ref, atol=5e-2, rtol=2e-2)
+
+
+@pytest.mark.parametrize("M,I,K", [(1, 384, 1024), (8, 1792, 4096), (48, 704, 2048), (300, 3072, 1024)])
+def test_gemm_swiglu(M, I, K):
+    from braidinfer_b200.ops.linear import interleave_gate_up, swiglu_ref_from_interleaved
+    x = torch.randn(M, K, device=DEV).bfloat16()
+    wg = (torch.randn(I, K, device=DEV) * 0.05).bfloat16()
+    wu = (torch.randn(I, K, device=DEV) * 0.05).bfloat16()
+    w = interleave_gate_up(wg, wu)
+    out = torch.empty(M, w.shape[0] // 2, device=DEV, dtype=torch.bfloat16)
+    _ext().gemm(out, x, w, None, None, 1)
+    ref = swiglu_ref_from_interleaved(x.float() @ w.float().t(), torch.bfloat16)
+    torch.testing.assert_close(out.float(), ref.float(), atol=3e-2, rtol=3e-2)
+    direct = torch.nn.functional.silu(x.float() @ wg.float().t()) * (x.float() @ wu.float().t())
+    torch.testing.assert_close(out.float()[:, :I], direct, atol=5e-2, rtol=5e-2)
+
+
+def test_rmsnorm_and_add():
+    from braidinfer_b200.ops.norm import rms_norm_ref
+    for H in (256, 1024, 4096, 8192):
+        x = torch.randn(13, H, device=DEV).bfloat16()
+        w = (torch.rand(H, device=DEV) * 2).bfloat16()
+        out = torch.empty_like(x)
+        _ext().rms_norm(out, x, w, 1e-6)
+        torch.testing.assert_close(out.float(), rms_norm_ref(x, w, 1e-6).float(), atol=2e-2, rtol=1e-2)
+        res = torch.randn(13, H, device=DEV).bfloat16()
+        res0 = res.clone()
+        _ext().add_rms_norm(out, res, x, w, 1e-6)
+        s = (res0.float() + x.float()).bfloat16()
+        torch.testing.assert_close(res.float(), s.float())
+        torch.testing.assert_close(out.float(), rms_norm_ref(s, w, 1e-6).float(), atol=2e-2, rtol=1e-2)
+
+
+def test_embedding_vocab_parallel():
+    w = torch.randn(100, 256, device=DEV).bfloat16()
+    ids = torch.tensor([0, 5, 99, 100, 150, 120], device=DEV, dtype=torch.int32)
+    out = torch.empty(6, 256, device=DEV, dtype=torch.bfloat16)
+    _ext().embedding(out, ids, w, 50)
+    ref = torch.zeros(6, 256, device=DEV, dtype=torch.bfloat16)
+    for i, t in enumerate(ids.tolist()):
+        if 50 <= t < 150:
+            ref[i] = w[t - 50]
+    assert torch.equal(out, ref)
+
+
+@pytest.mark.parametrize("D,qk_norm", [(64, False), (128, True)])
+def test_qkv_prepare(D, qk_norm):
+    from braidinfer_b200 import ops
+    T, Hq, Hkv, PS, P = 37, 8, 2, 16, 8
+    qkv = torch.randn(T, (Hq + 2 * Hkv) * D, device=DEV).bfloat16()
+    pos = torch.randint(0, 500, (T,), device=DEV, dtype=torch.int32)
+    slots = torch.randperm(P * PS, device=DEV)[:T].int()
+    cos, sin = ops.build_cos_sin(D, 10000.0, 1024, device=DEV)
+    qn = (torch.rand(D, device=DEV) * 3).bfloat16() if qk_norm else None
+    kn = (torch.rand(D, device=DEV) * 100 - 50).bfloat16() if qk_norm else None
+    kv = torch.zeros(P, 2, Hkv, PS, D, device=DEV, dtype=torch.bfloat16)
+    kv_ref = kv.clone().float()
+    q = ops.qkv_prepare(qkv, pos, slots, kv, Hq, Hkv, D, cos, sin, qn, kn, 1e-6, True)
+    q_ref = ops.qkv_prepare(qkv.float().cpu(), pos.cpu(), slots.cpu(), kv_ref.cpu(), Hq, Hkv, D, cos.cpu(),
+                            sin.cpu(), None if qn is None else qn.cpu(), None if kn is None else kn.cpu(), 1e-6, True)
+    torch.testing.assert_close(q.float().cpu(), q_ref.float(), atol=3e-2 * (50 if qk_norm else 1), rtol=2e-2)
+
+
+def _rand_plan(seqs, PS, P, device, decode):
+    """seqs: list of (q_len, [(seg_len, offset, delta)]) -> (meta tensors host dict, T)."""
+    import numpy as np
+    from braidinfer_b200.ops.attention import AttnMeta
+    rng = np.random.default_rng(0)
+    free = list(rng.permutation(P))
+    qo, segi, spi, soff, slen, spos0, sdelta, pids, pos = [0], [0], [0], [], [], [], [], [], []
+    for qlen, segs in seqs:
+        p = 0
+        for (n, off, delta) in segs:
+            npg = -(-(off + n) // PS)
+            pids += [free.pop() for _ in range(npg)]
+            spi.append(len(pids)); soff.append(off); slen.append(n); spos0.append(p); sdelta.append(delta)
+            p += n
+        pos += list(range(p - qlen, p))
+        qo.append(qo[-1] + qlen)
+        segi.append(len(slen))
+    host = {k: torch.tensor(v, dtype=torch.int32) for k, v in dict(
+        qo_indptr=qo, positions=pos, seg_indptr=segi, seg_page_indptr=spi, seg_offset=soff, seg_len=slen,
+        seg_pos0=spos0, seg_delta=sdelta, page_ids=pids).items()}
+    dev = {k: v.to(device) for k, v in host.items()}
+    maxq = max(q for q, _ in seqs)
+    maxkv = max(sum(s[0] for s in segs) for _, segs in seqs)
+    meta = AttnMeta(num_seqs=len(seqs), max_q_len=maxq, max_kv_len=maxkv, decode=decode, host=host, **dev)
+    return meta, qo[-1]
+
+
+@pytest.mark.parametrize("D,G", [(64, 8), (128, 2), (128, 4), (128, 8)])
+@pytest.mark.parametrize("splits", [1, 3])
+def test_attention_decode(D, G, splits):
+    from braidinfer_b200 import ops
+    PS, P, Hkv = 16, 512, 2
+    Hq = Hkv * G
+    seqs = [(1, [(37, 0, 5), (100, 3, -7), (9, 0, 0)]), (1, [(1, 0, 0)]), (1, [(300, 0, 0)]),
+            (1, [(64, 0, 2), (64, 0, 0), (130, 0, 0)])]
+    meta, T = _rand_plan(seqs, PS, P, DEV, True)
+    meta.num_splits = splits
+    kv = torch.randn(P, 2, Hkv, PS, D, device=DEV).bfloat16()
+    q = torch.randn(T, Hq, D, device=DEV).bfloat16()
+    cos, sin = ops.build_cos_sin(D, 10000.0, 2048, device=DEV)
+    out = ops.attention(q, kv, meta, cos, sin, D ** -0.5, True)
+    ref = ops.attention_ref(q.cpu().float(), kv.cpu().float(), meta, cos.cpu(), sin.cpu(), D ** -0.5, True)
+    torch.testing.assert_close(out.float().cpu(), ref.float(), atol=2e-2, rtol=2e-2)
+
+
+@pytest.mark.parametrize("D,G", [(64, 8), (128, 2), (128, 4)])
+def test_attention_prefill(D, G):
+    from braidinfer_b200 import ops
+    PS, P, Hkv = 16, 1024, 2
+    Hq = Hkv * G
+    # (q_len, segments): last segment is the private one holding the queries
+    seqs = [(50, [(40, 0, 3), (70, 5, -11), (50, 0, 0)]), (1, [(1, 0, 0)]), (200, [(200, 0, 0)]),
+            (17, [(128, 0, 0), (33, 0, 0)])]
+    meta, T = _rand_plan(seqs, PS, P, DEV, False)
+    kv = torch.randn(P, 2, Hkv, PS, D, device=DEV).bfloat16()
+    q = torch.randn(T, Hq, D, device=DEV).bfloat16()
+    cos, sin = ops.build_cos_sin(D, 10000.0, 2048, device=DEV)
+    out = ops.attention(q, kv, meta, cos, sin, D ** -0.5, True)
+    ref = ops.attention_ref(q.cpu().float(), kv.cpu().float(), meta, cos.cpu(), sin.cpu(), D ** -0.5, True)
+    torch.testing.assert_close(out.float().cpu(), ref.float(), atol=2e-2, rtol=2e-2)
+
+
+def test_sampler_greedy_and_filters():
+    from braidinfer_b200.ops.sampling import sample_ref
+    B, V = 6, 50000
+    logits = torch.randn(B, V, device=DEV) * 3
+    temp = torch.tensor([0.0, 1.0, 0.7, 1.0, 1.3, 0.5], device=DEV)
+    topk = torch.tensor([0, 0, 5, 1, 0, 50], device=DEV, dtype=torch.int32)
+    topp = torch.tensor([1.0, 1.0, 1.0, 1.0, 0.5, 0.9], device=DEV)
+    minp = torch.tensor([0.0, 0.0, 0.0, 0.0, 0.0, 0.1], device=DEV)
+    seed = torch.arange(B, device=DEV, dtype=torch.int64) + 11
+    step = torch.full((B,), 3, device=DEV, dtype=torch.int64)
+    out = torch.empty(B, dtype=torch.int32, device=DEV)
+    _ext().sample(out, logits, temp, topk, topp, minp, seed, step, False)
+    ref = sample_ref(logits.cpu(), temp.cpu(), topk.cpu(), topp.cpu(), minp.cpu(), seed.cpu(), step.cpu())
+    assert out[0].item() == logits[0].argmax().item()
+    assert out[3].item() == logits[3].argmax().item()  # top_k = 1
+    top5 = set(logits[2].topk(5).indices.tolist())
+    assert out[2].item() in top5
+    # same hash on both sides: identical draws
+    assert out.cpu().tolist() == ref.tolist()
