@@ -218,14 +218,30 @@ def run_reference(args) -> None:
     sys.path.insert(0, ref)
     import torch
 
-    d = make_config_dir(args.model, with_weights=True)
     from braidinfer import LLM, SamplingParams  # the unmodified reference
+    from braidinfer.engine.errors import ModelLoadError
 
+    kw = dict(num_kvcache_blocks=-(-(args.prompt_len + args.warmup + args.steps + 64) // 256) + 4,
+              max_model_len=args.prompt_len + args.warmup + args.steps + 64)
+    # Model construction happens before any weight is read, so try it on the
+    # config-only directory first and report an incompatibility without
+    # writing the 16 GB checkpoint.
+    try:
+        LLM(make_config_dir(args.model, with_weights=False), **kw)
+    except ModelLoadError as e:
+        msg = str(e)
+        if "Failed to create model instance" in msg:
+            print(json.dumps({"impl": "reference", "unavailable":
+                              f"reference model construction fails in this image: {msg} (its lru_cache'd "
+                              "get_rope receives transformers 5.5's rope_scaling dict)"}), flush=True)
+            return
+    except Exception:
+        pass
+    d = make_config_dir(args.model, with_weights=True)
     # The reference raises NotImplementedError for batch > 1
     # (braidinfer/layers/attention.py:146-147), so the batch's requests run one
     # after another through its public generate(stream=True) API.
-    llm = LLM(d, num_kvcache_blocks=-(-(args.prompt_len + args.warmup + args.steps + 64) // 256) + 4,
-              max_model_len=args.prompt_len + args.warmup + args.steps + 64)
+    llm = LLM(d, **kw)
     prompts = prompts_for(args.batch, args.prompt_len, llm.config.hf_config.vocab_size)
     sp = SamplingParams(temperature=0.0, max_tokens=args.warmup + args.steps + 1, ignore_eos=True)
     import contextlib

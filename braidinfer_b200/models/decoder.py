@@ -13,10 +13,13 @@ embedding scaling for Qwen3 (``braidinfer/models/qwen3.py:465``), ``lm_head``
 tied to ``embed_tokens`` when ``tie_word_embeddings`` is set, K cached after
 k_norm and RoPE and never re-normalised at attention time.
 
-Per layer the forward runs: RMSNorm → QKV GEMM (+bias) → fused q/k-norm +
-RoPE(k) + paged KV append → cascade attention (query-side differential RoPE)
-→ o_proj GEMM with the residual add in its epilogue (or the TP reduction) →
-RMSNorm → gate/up GEMM with SwiGLU in its epilogue → down GEMM + residual.
+Per layer the forward runs five kernels: QKV GEMM (input RMSNorm fused: the
+norm weight is folded into the weight columns at load time and each token's
+1/rms is applied in the epilogue, then bias, q/k-norm, RoPE(k) and the paged
+KV append) → cascade attention (query-side differential RoPE) → o_proj GEMM
+with the residual add in its epilogue (or the TP reduction) → gate/up GEMM
+(post-attention RMSNorm fused the same way, SwiGLU in the epilogue) → down
+GEMM + residual.  The final norm is folded into a copy of the LM head.
 """
 from __future__ import annotations
 
@@ -81,6 +84,8 @@ class DecoderLM:
         self.embed = torch.empty(L.vocab_local, H, **kw)
         self.final_norm = torch.ones(H, **kw)
         self.lm_head = self.embed if spec.tie_word_embeddings else torch.empty(L.vocab_local, H, **kw)
+        self.lm_head_folded = None  # lm_head * final_norm, built by finalize()
+        self.finalized = False
         # RoPE tables: room for query positions shifted by chunk deltas.
         self.rope_len = 2 * max_pos + 16
         if spec.use_rope:
@@ -195,6 +200,23 @@ class DecoderLM:
             return False
         return True
 
+    def finalize(self) -> None:
+        """Fold each RMSNorm weight into the columns of the GEMM that consumes
+        the normalised activations (``W' = W diag(g)``); the GEMM epilogue then
+        only scales each token's row by ``1/rms(x)``.  Called once after the
+        weights are loaded or initialised."""
+        if self.finalized:
+            return
+
+        def fold(wt, g):
+            wt.copy_((wt.float() * g.float()[None, :]).to(wt.dtype))
+
+        for w in self.layers:
+            fold(w.qkv_w, w.in_norm)
+            fold(w.gu_w, w.post_norm)
+        self.lm_head_folded = (self.lm_head.float() * self.final_norm.float()[None, :]).to(self.dtype)
+        self.finalized = True
+
     # --------------------------------------------------------------- forward
     def embed_tokens(self, input_ids: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
         h = ops.embedding(input_ids, self.embed, self.layout.vocab_start)
@@ -206,40 +228,31 @@ class DecoderLM:
                 meta, kv_cache: torch.Tensor, workspace: Optional[Dict] = None) -> torch.Tensor:
         """Return the residual stream ``[T, hidden]`` after the last layer (pre final norm)."""
         S, L = self.spec, self.layout
+        assert self.finalized, "call finalize() after loading weights"
+        eps = S.rms_norm_eps
         residual = self.embed_tokens(input_ids, positions)
-        x = ops.rms_norm(residual, self.layers[0].in_norm, S.rms_norm_eps)
-        n = len(self.layers)
         for i, w in enumerate(self.layers):
-            qkv = ops.linear(x, w.qkv_w, w.qkv_b)
-            q = ops.qkv_prepare(qkv, positions, slot_mapping, kv_cache[i], L.q_heads, L.kv_heads, S.head_dim,
-                                self.cos, self.sin, w.q_norm, w.k_norm, S.rms_norm_eps, S.use_rope)
+            q = ops.qkv_gemm(residual, w.qkv_w, w.qkv_b, eps, positions, slot_mapping, kv_cache[i], L.q_heads,
+                             L.kv_heads, S.head_dim, self.cos, self.sin, w.q_norm, w.k_norm, eps, S.use_rope)
             o = ops.attention(q, kv_cache[i], meta, self.cos, self.sin, self.scale, S.use_rope, workspace)
             if self.tp.size == 1:
-                residual = ops.linear(o, w.o_w, residual=residual)
-                x = ops.rms_norm(residual, w.post_norm, S.rms_norm_eps)
+                residual = ops.linear(o, w.o_w, residual=residual, out=residual)
             else:
-                x, residual = comm.all_reduce_add_rms_norm(ops.linear(o, w.o_w), residual, w.post_norm,
-                                                           S.rms_norm_eps)
-            g = ops.linear_swiglu(x, w.gu_w)
-            nxt = self.layers[i + 1].in_norm if i + 1 < n else None
+                residual = comm.all_reduce_add(ops.linear(o, w.o_w), residual)
+            g = ops.linear_swiglu(residual, w.gu_w, rms_eps=eps)
             if self.tp.size == 1:
-                residual = ops.linear(g, w.down_w, residual=residual)
-                if nxt is not None:
-                    x = ops.rms_norm(residual, nxt, S.rms_norm_eps)
+                residual = ops.linear(g, w.down_w, residual=residual, out=residual)
             else:
-                if nxt is not None:
-                    x, residual = comm.all_reduce_add_rms_norm(ops.linear(g, w.down_w), residual, nxt,
-                                                               S.rms_norm_eps)
-                else:
-                    residual = residual + comm.all_reduce(ops.linear(g, w.down_w))
+                residual = comm.all_reduce_add(ops.linear(g, w.down_w), residual)
         return residual
 
     def final_hidden(self, h: torch.Tensor) -> torch.Tensor:
-        return ops.rms_norm(h, self.final_norm, self.spec.rms_norm_eps)
+        """Rows fed to the LM head; the final RMSNorm is fused into ``compute_logits``."""
+        return h
 
-    def compute_logits(self, hn: torch.Tensor) -> torch.Tensor:
-        """Full-vocabulary logits ``[B, V]`` from final-normed rows ``hn``."""
-        local = ops.linear(hn, self.lm_head)
+    def compute_logits(self, h: torch.Tensor) -> torch.Tensor:
+        """Full-vocabulary logits ``[B, V]`` from residual-stream rows ``h``."""
+        local = ops.linear(h, self.lm_head_folded, rms_eps=self.spec.rms_norm_eps)
         if self.tp.size > 1:
             return comm.all_gather_last(local, self.spec.vocab_size)
         return local

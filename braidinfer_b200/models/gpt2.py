@@ -114,6 +114,9 @@ class GPT2LM:
             return False
         return True
 
+    def finalize(self) -> None:
+        pass
+
     def embed_tokens(self, input_ids, positions):
         h = ops.embedding(input_ids, self.embed, self.layout.vocab_start)
         if self.tp.size > 1:

@@ -89,6 +89,28 @@ def qkv_prepare(qkv: torch.Tensor, positions: torch.Tensor, slot_mapping: torch.
     return q.contiguous()
 
 
+def qkv_gemm(x: torch.Tensor, w_qkv: torch.Tensor, bias: Optional[torch.Tensor], rms_eps: Optional[float],
+             positions: torch.Tensor, slot_mapping: torch.Tensor, kv_layer: torch.Tensor, num_q_heads: int,
+             num_kv_heads: int, head_dim: int, cos: torch.Tensor, sin: torch.Tensor,
+             q_norm: Optional[torch.Tensor] = None, k_norm: Optional[torch.Tensor] = None, eps: float = 1e-6,
+             use_rope: bool = True) -> torch.Tensor:
+    """QKV projection (fused input RMSNorm when ``rms_eps`` is set, norm weight
+    folded into ``w_qkv``) with the q/k-norm, RoPE(k) and paged KV append done
+    in the GEMM epilogue on CUDA.  Returns unrotated q ``[T, Hq, D]``."""
+    T = x.shape[0]
+    if x.is_cuda:
+        q = torch.empty(T, num_q_heads, head_dim, dtype=x.dtype, device=x.device)
+        ext().gemm_qkv(q, x, w_qkv, bias, -1.0 if rms_eps is None else float(rms_eps), positions, slot_mapping,
+                       kv_layer, q_norm, k_norm, float(eps), cos, sin, num_q_heads, num_kv_heads, head_dim,
+                       bool(use_rope))
+        return q
+    from .linear import linear
+
+    qkv = linear(x, w_qkv, bias, rms_eps=rms_eps)
+    return qkv_prepare(qkv, positions, slot_mapping, kv_layer, num_q_heads, num_kv_heads, head_dim, cos, sin,
+                       q_norm, k_norm, eps, use_rope)
+
+
 def attention_ref(q: torch.Tensor, kv_layer: torch.Tensor, meta: AttnMeta, cos: torch.Tensor,
                   sin: torch.Tensor, scale: float, use_rope: bool = True) -> torch.Tensor:
     """fp32 restatement of the cascade kernel (one softmax over all segments)."""

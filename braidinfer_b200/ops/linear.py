@@ -30,14 +30,32 @@ def _round(t: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     return t.to(dtype).float() if dtype != torch.float32 else t
 
 
+def _rstd(x: torch.Tensor, eps: float) -> torch.Tensor:
+    xf = x.float()
+    return torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+
+
+def _acc(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor], rms_eps: Optional[float]) -> torch.Tensor:
+    y = F.linear(x.float(), w.float())
+    if rms_eps is not None:
+        y = y * _rstd(x, rms_eps)
+    if bias is not None:
+        y = y + bias.float()
+    return y
+
+
 def linear(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None,
-           residual: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+           residual: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+           rms_eps: Optional[float] = None) -> torch.Tensor:
+    """``y = x @ w.T (+bias) (+residual)``.  With ``rms_eps`` the input is
+    RMS-normalised on the fly: ``w`` must already carry the norm weight folded
+    into its columns, and ``1/rms(x_t)`` scales each token's row."""
     if x.is_cuda:
         M = x.shape[0]
         out = torch.empty(M, w.shape[0], dtype=x.dtype, device=x.device) if out is None else out
-        ext().gemm(out, x, w, bias, residual, 0)
+        ext().gemm(out, x, w, bias, residual, 0, -1.0 if rms_eps is None else float(rms_eps))
         return out
-    y = F.linear(x.float(), w.float(), None if bias is None else bias.float())
+    y = _acc(x, w, bias, rms_eps)
     if residual is not None:
         y = _round(y, x.dtype) + residual.float()
     y = y.to(x.dtype)
@@ -68,14 +86,15 @@ def swiglu_ref_from_interleaved(y: torch.Tensor, dtype: torch.dtype, block: int 
     return (s * u).reshape(M, N2 // 2).to(dtype)
 
 
-def linear_swiglu(x: torch.Tensor, w_gu: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+def linear_swiglu(x: torch.Tensor, w_gu: torch.Tensor, out: Optional[torch.Tensor] = None,
+                  rms_eps: Optional[float] = None) -> torch.Tensor:
     """``silu(x @ Wg.T) * (x @ Wu.T)`` from the block-interleaved ``w_gu``."""
     if x.is_cuda:
         M = x.shape[0]
         out = torch.empty(M, w_gu.shape[0] // 2, dtype=x.dtype, device=x.device) if out is None else out
-        ext().gemm(out, x, w_gu, None, None, 1)
+        ext().gemm(out, x, w_gu, None, None, 1, -1.0 if rms_eps is None else float(rms_eps))
         return out
-    y = F.linear(x.float(), w_gu.float())
+    y = _acc(x, w_gu, None, rms_eps)
     r = swiglu_ref_from_interleaved(y, x.dtype)
     if out is not None:
         out.copy_(r)

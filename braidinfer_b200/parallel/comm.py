@@ -37,6 +37,16 @@ def all_reduce(x: torch.Tensor) -> torch.Tensor:
     return x
 
 
+def all_reduce_add(partial: torch.Tensor, residual: torch.Tensor) -> torch.Tensor:
+    """``residual += sum_ranks(partial)`` (activation dtype), returns residual."""
+    tp = get_tp()
+    if tp.size > 1 and _fused is not None and partial.is_cuda and _fused.can_all_reduce(partial):
+        return _fused.all_reduce_add(partial, residual)
+    s = all_reduce(partial)
+    residual.copy_((residual.float() + s.float()).to(residual.dtype))
+    return residual
+
+
 def all_reduce_add_rms_norm(partial: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float,
                             out: Optional[torch.Tensor] = None):
     """``residual += sum_ranks(partial)``; return ``(rms_norm(residual), residual)``."""

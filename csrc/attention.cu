@@ -19,8 +19,9 @@
 // fragments.  Rows of the Q tile are (query token, head-in-KV-group) pairs, so
 // one K/V tile serves every query head that shares the KV head.
 //   decode  : grid (seq, kv_head, split); the 4 warps split each 64-key tile,
-//             partial states merged in shared memory, then across splits by
-//             attn_merge_kernel (log-sum-exp weights).
+//             partial states merged in shared memory; with several splits the
+//             last-arriving split CTA of a (token, kv head) merges all splits
+//             (log-sum-exp weights) from a fp32 scratch, so no merge launch.
 //   prefill : grid (64-row q tile, seq, kv_head); each warp owns 16 rows and
 //             walks every tile; key tiles beyond the tile's last query
 //             position are skipped.
@@ -29,6 +30,10 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include "common.cuh"
+#include "launch.cuh"
+
+#include <mutex>
+#include <unordered_map>
 
 namespace braid {
 
@@ -54,6 +59,7 @@ struct AttnParams {
   int num_splits;
   float* part_o;    // [T, Hq, splits, D]
   float* part_lse;  // [T, Hq, splits]
+  int* counters;    // [T * Hkv] split arrival counters, kept at zero between launches
 };
 
 constexpr float LOG2E = 1.4426950408889634f;
@@ -221,6 +227,8 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnParams p) {
   uint8_t* vbuf = kbuf + 2 * KT * D * 2;             // 2 x [64][D]
   const int b = blockIdx.x, kh = blockIdx.y, split = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_wait();
+  pdl_trigger();
   const int t = p.qo_indptr[b];
   if (p.qo_indptr[b + 1] - t < 1) return;
   const int qpos = p.positions[t];
@@ -323,25 +331,35 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnParams p) {
       if (d == 0) p.part_lse[idx] = L > 0.f ? M + log2f(L) : -INFINITY;
     }
   }
-}
-
-template <int D>
-__global__ void attn_merge_kernel(const AttnParams p, int T) {
-  const int t = blockIdx.x, h = blockIdx.y;
+  if (p.num_splits == 1) return;
+  // ---- the last split CTA of (token, kv head) merges every split's partial
+  __shared__ int s_last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int* c = p.counters + (size_t)t * p.Hkv + kh;
+    const int old = atomicAdd(c, 1);
+    s_last = old == p.num_splits - 1;
+    if (s_last) *c = 0;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
   const int ns = p.num_splits;
-  const size_t base = ((size_t)t * p.Hq + h) * ns;
-  float M = -INFINITY;
-  for (int s = 0; s < ns; ++s) M = fmaxf(M, p.part_lse[base + s]);
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+    const int row = i / D, d = i % D;
+    const size_t base = ((size_t)t * p.Hq + kh * G + row) * ns;
+    float M = -INFINITY;
+    for (int s = 0; s < ns; ++s) M = fmaxf(M, __ldcg(p.part_lse + base + s));
     float W = 0.f, O = 0.f;
     if (M != -INFINITY) {
       for (int s = 0; s < ns; ++s) {
-        const float w = exp2f(p.part_lse[base + s] - M);
+        const float w = exp2f(__ldcg(p.part_lse + base + s) - M);
         W += w;
-        O += w * p.part_o[(base + s) * D + d];
+        O += w * __ldcg(p.part_o + (base + s) * D + d);
       }
     }
-    p.out[(size_t)t * p.Hq * D + h * D + d] = f2bf(W > 0.f ? O / W : 0.f);
+    p.out[(size_t)t * p.Hq * D + (kh * G + row) * D + d] = f2bf(W > 0.f ? O / W : 0.f);
   }
 }
 
@@ -354,6 +372,8 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const AttnParams p) {
   uint8_t* vbuf = kbuf + 2 * KT * D * 2;
   const int b = blockIdx.y, kh = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_wait();
+  pdl_trigger();
   const int G = p.G;
   const int t0 = p.qo_indptr[b], nt = p.qo_indptr[b + 1] - t0;
   const int rows = nt * G;
@@ -447,25 +467,44 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const AttnParams p) {
 }
 
 // ------------------------------------------------------------------ host
+// Per-device split-merge counters (zeroed once; the merging CTA re-arms its counter).
+static int* attn_counters(int dev, size_t n) {
+  static std::mutex mu;
+  static std::unordered_map<int, std::pair<int*, size_t>> all;
+  std::lock_guard<std::mutex> g(mu);
+  auto& e = all[dev];
+  if (n > e.second) {
+    // growth happens only outside graph capture (warm-up runs the same shapes first)
+    if (e.first) C10_CUDA_CHECK(cudaFree(e.first));
+    const size_t m = std::max(n, (size_t)1 << 16);
+    C10_CUDA_CHECK(cudaMalloc(&e.first, m * sizeof(int)));
+    C10_CUDA_CHECK(cudaMemset(e.first, 0, m * sizeof(int)));
+    e.second = m;
+  }
+  return e.first;
+}
+
 template <int D>
 static void launch_attn(AttnParams& p, int num_seqs, int max_q_len, bool decode, int T, cudaStream_t st) {
   if (decode) {
     const int smem = 16 * D * 2 + 4 * KT * D * 2;
     auto k = attn_decode_kernel<D>;
-    C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    k<<<dim3(num_seqs, p.Hkv, p.num_splits), 128, smem, st>>>(p);
-    C10_CUDA_KERNEL_LAUNCH_CHECK();
-    if (p.num_splits > 1) {
-      attn_merge_kernel<D><<<dim3(T, p.Hq), D, 0, st>>>(p, T);
-      C10_CUDA_KERNEL_LAUNCH_CHECK();
+    static bool attr = false;
+    if (!attr) {
+      C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      attr = true;
     }
+    launch_pdl(k, dim3(num_seqs, p.Hkv, p.num_splits), dim3(128), smem, st, p);
   } else {
     const int smem = 64 * D * 2 + 4 * KT * D * 2;
     auto k = attn_prefill_kernel<D>;
-    C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    static bool attr = false;
+    if (!attr) {
+      C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      attr = true;
+    }
     const int qt = (max_q_len * p.G + 63) / 64;
-    k<<<dim3(qt, num_seqs, p.Hkv), 128, smem, st>>>(p);
-    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    launch_pdl(k, dim3(qt, num_seqs, p.Hkv), dim3(128), smem, st, p);
   }
 }
 
@@ -519,6 +558,7 @@ void attention(torch::Tensor out, torch::Tensor q, torch::Tensor kv, torch::Tens
     }
     p.part_o = po.data_ptr<float>();
     p.part_lse = pl.data_ptr<float>();
+    p.counters = attn_counters(q.get_device(), (size_t)T * Hkv);
   }
   if (D == 128)
     launch_attn<128>(p, num_seqs, max_q_len, decode, T, st);

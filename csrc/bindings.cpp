@@ -3,7 +3,11 @@
 
 namespace braid {
 void gemm(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
-          c10::optional<torch::Tensor> residual, int64_t epi);
+          c10::optional<torch::Tensor> residual, int64_t epi, double rs_eps);
+void gemm_qkv(torch::Tensor q_out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
+              double rs_eps, torch::Tensor positions, torch::Tensor slots, torch::Tensor kv,
+              c10::optional<torch::Tensor> q_norm, c10::optional<torch::Tensor> k_norm, double head_eps,
+              torch::Tensor cos, torch::Tensor sin, int64_t Hq, int64_t Hkv, int64_t D, bool use_rope);
 int64_t gemm_check_error(int64_t device);
 void attention(torch::Tensor out, torch::Tensor q, torch::Tensor kv, torch::Tensor qo_indptr,
                torch::Tensor positions, torch::Tensor seg_indptr, torch::Tensor seg_page_indptr,
@@ -27,6 +31,7 @@ void sample(torch::Tensor out, torch::Tensor logits, torch::Tensor temperature, 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "braidinfer_b200 native sm_100a kernels";
   m.def("gemm", &braid::gemm, "tcgen05 GEMM out = x @ w^T (+bias)(+residual); epi 1 = SwiGLU");
+  m.def("gemm_qkv", &braid::gemm_qkv, "tcgen05 QKV GEMM with fused q/k-norm, RoPE(k) and paged KV append");
   m.def("gemm_check_error", &braid::gemm_check_error, "read and clear the GEMM bounded-wait error flag");
   m.def("attention", &braid::attention, "paged cascade attention (decode/prefill)");
   m.def("rms_norm", &braid::rms_norm);

@@ -73,6 +73,12 @@ BRAID_DEVICE bool mbar_wait(uint64_t* bar, uint32_t phase, uint64_t timeout_ns =
     if (globaltimer_ns() - t0 > timeout_ns) return false;
   }
 }
+// Programmatic dependent launch: wait until the preceding grid in the stream
+// has completed and its memory is visible (no-op without the PDL attribute);
+// allow the next grid to begin launching.
+BRAID_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+BRAID_DEVICE void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 BRAID_DEVICE void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }

@@ -12,6 +12,7 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include "common.cuh"
+#include "launch.cuh"
 
 namespace braid {
 

@@ -35,40 +35,107 @@
 #include <vector>
 
 #include "common.cuh"
+#include "launch.cuh"
 
 namespace braid {
+
+// Fused QKV epilogue (epi == 2): per-head q/k RMSNorm, RoPE on k, q written
+// unrotated to q_out, k/v appended to the paged KV cache at slots[token].
+struct QkvEpi {
+  __nv_bfloat16* q_out;  // [T, Hq, D]
+  __nv_bfloat16* kv;     // layer cache [P, 2, Hkv, PS, D]
+  const int* slots;
+  const int* positions;
+  const __nv_bfloat16* q_norm;
+  const __nv_bfloat16* k_norm;
+  const float* cos;
+  const float* sin;
+  int Hq, Hkv, D, PS, use_rope;
+  float eps;
+};
 
 struct GemmArgs {
   int M, N, K;        // A rows, B rows, reduction length
   int swap;           // 1: A is the weight, output written transposed
-  int epi;            // 0 plain, 1 swiglu
+  int epi;            // 0 plain, 1 swiglu, 2 qkv
   __nv_bfloat16* out;
   int ldo;
   const __nv_bfloat16* bias;      // indexed by feature
   const __nv_bfloat16* residual;  // same layout as out
   int ldr;
+  // Fused input RMSNorm: the norm weight is folded into the weight matrix and
+  // each token's 1/rms(x) is applied here (x = the activation operand).
+  const __nv_bfloat16* rs_x;
+  int rs_ld;
+  float rs_eps;
   int splits;
   int kb_per_split;
   float* ws;          // split-K partials
   int* counters;      // one per output tile, kept at zero between launches
   int* err;           // error flag (bounded-wait timeout)
+  QkvEpi qkv;
 };
 
 constexpr int BM = 128;
 constexpr int BK = 64;
+constexpr int XCH_LD = 17;  // exchange tile: 128 rows x 16 columns (+1 pad) fp32
 
 template <int BN, int STAGES>
 struct GemmSmem {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int RING = STAGES * (A_BYTES + B_BYTES);
-  static constexpr int XCH = BN <= 64 ? 64 * (BN + 1) * 4 : 0;  // swapped-SwiGLU exchange
-  static constexpr int BAR_OFF = RING + XCH;
+  static constexpr int XCH = BM * XCH_LD * 4;
+  static constexpr int RSTD = 256 * 4;
+  static constexpr int BAR_OFF = RING + XCH + RSTD;
   static constexpr int TOTAL = BAR_OFF + (2 * STAGES + 1) * 8 + 16 + 1024;  // +1024 alignment slack
 };
 
+// Per-head q/k norm + RoPE on E = D/32 consecutive dims held by this lane;
+// the rotary partner of dim e (< D/2) is e + D/2, held by lane ^ 16.
+template <int E>
+BRAID_DEVICE void qkv_head_store(const QkvEpi& q, float* v, int head, int t, int lane) {
+  const int D = E * 32;
+  const bool is_q = head < q.Hq, is_k = !is_q && head < q.Hq + q.Hkv;
+  const __nv_bfloat16* nw = is_q ? q.q_norm : (is_k ? q.k_norm : nullptr);
+  if (nw != nullptr) {
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < E; ++i) ss += v[i] * v[i];
+    const float r = rsqrtf(warp_sum(ss) / D + q.eps);
+#pragma unroll
+    for (int i = 0; i < E; ++i) v[i] = rbf(rbf(v[i] * r) * bf2f(nw[lane * E + i]));
+  }
+  if (is_q) {
+    __nv_bfloat16* dst = q.q_out + ((size_t)t * q.Hq + head) * D + lane * E;
+#pragma unroll
+    for (int i = 0; i < E; ++i) dst[i] = f2bf(v[i]);
+    return;
+  }
+  if (is_k && q.use_rope) {
+    const int pos = q.positions[t];
+    float pr[E];
+#pragma unroll
+    for (int i = 0; i < E; ++i) pr[i] = __shfl_xor_sync(0xffffffffu, v[i], 16);
+    const bool first = lane < 16;
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+      const int d = (lane & 15) * E + i;
+      const float c = q.cos[(size_t)pos * (D / 2) + d], s = q.sin[(size_t)pos * (D / 2) + d];
+      v[i] = first ? v[i] * c - pr[i] * s : v[i] * c + pr[i] * s;
+    }
+  }
+  const int slot = q.slots[t];
+  const int page = slot / q.PS, off = slot % q.PS;
+  const int kh = is_k ? head - q.Hq : head - q.Hq - q.Hkv;
+  __nv_bfloat16* dst =
+      q.kv + ((((size_t)page * 2 + (is_k ? 0 : 1)) * q.Hkv + kh) * q.PS + off) * D + lane * E;
+#pragma unroll
+  for (int i = 0; i < E; ++i) dst[i] = f2bf(v[i]);
+}
+
 template <int BN, int STAGES>
-__global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
+__global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
                                                                const __grid_constant__ CUtensorMap tmB,
                                                                const GemmArgs args) {
   using S = GemmSmem<BN, STAGES>;
@@ -77,6 +144,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_const
   uint8_t* ringA = smem;
   uint8_t* ringB = smem + STAGES * S::A_BYTES;
   float* xch = reinterpret_cast<float*>(smem + S::RING);
+  float* rstd_s = reinterpret_cast<float*>(smem + S::RING + S::XCH);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
   uint64_t* empty = full + STAGES;
   uint64_t* tmem_full = empty + STAGES;
@@ -110,10 +178,20 @@ __global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_const
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {
-      for (int i = 0; i < nkb; ++i) {
+      // The weight operand does not depend on the preceding kernel: start
+      // streaming it before the dependency wait (swapped mode: A is the weight).
+      const int pre = args.swap ? min(nkb, STAGES) : 0;
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(&full[i], S::A_BYTES + S::B_BYTES);
+        tma_load_2d(ringA + i * S::A_BYTES, &tmA, &full[i], (kb0 + i) * BK, m0);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i) tma_load_2d(ringB + i * S::B_BYTES, &tmB, &full[i], (kb0 + i) * BK, n0);
+      for (int i = pre; i < nkb; ++i) {
         const int s = i % STAGES;
         if (i >= STAGES && !mbar_wait(&empty[s], ((i / STAGES) & 1) ^ 1)) {
           atomicExch(args.err, 1);
@@ -128,12 +206,10 @@ __global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_const
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
-      bool ok = true;
       for (int i = 0; i < nkb; ++i) {
         const int s = i % STAGES;
         if (!mbar_wait(&full[s], (i / STAGES) & 1)) {
           atomicExch(args.err, 2);
-          ok = false;
           break;
         }
         tc_fence_after();
@@ -144,7 +220,6 @@ __global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_const
           tc_mma_bf16(tmem, ad + 2 * k, bd + 2 * k, idesc, (i | k) != 0 ? 1u : 0u);
         tc_commit(&empty[s]);
       }
-      (void)ok;
       tc_commit(tmem_full);
     }
   } else {
@@ -152,6 +227,43 @@ __global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_const
     const int wq = warp & 3;             // TMEM lane quarter this warp may access
     const int r = wq * 32 + lane;        // row of the tile owned by this thread
     const int et = threadIdx.x - 64;     // 0..127 epilogue thread id
+    const int ew = et >> 5;              // epilogue warp 0..3
+    pdl_wait();
+    // Fused input RMSNorm: 1/rms of every token of the tile (overlaps the mainloop).
+    float rs_row = 1.f;
+    if (args.rs_x != nullptr) {
+      if (args.swap) {
+        for (int tt = ew; tt < BN; tt += 4) {
+          const int t = n0 + tt;
+          float ss = 0.f;
+          if (t < args.N) {
+            const __nv_bfloat16* xr = args.rs_x + (size_t)t * args.rs_ld;
+            for (int k = lane * 8; k < args.K; k += 256) {
+              const uint4 u = *reinterpret_cast<const uint4*>(xr + k);
+              const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) ss += bf2f(e[j]) * bf2f(e[j]);
+            }
+          }
+          ss = warp_sum(ss);
+          if (lane == 0) rstd_s[tt] = rsqrtf(ss / args.K + args.rs_eps);
+        }
+        named_bar_sync(1, 128);
+      } else {
+        const int m = m0 + r;
+        if (m < args.M) {
+          const __nv_bfloat16* xr = args.rs_x + (size_t)m * args.rs_ld;
+          float ss = 0.f;
+          for (int k = 0; k < args.K; k += 8) {
+            const uint4 u = *reinterpret_cast<const uint4*>(xr + k);
+            const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) ss += bf2f(e[j]) * bf2f(e[j]);
+          }
+          rs_row = rsqrtf(ss / args.K + args.rs_eps);
+        }
+      }
+    }
     const bool ready = mbar_wait(tmem_full, 0);
     if (!ready) atomicExch(args.err, 3);
     tc_fence_after();
@@ -173,7 +285,8 @@ __global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_const
           for (int j = 0; j < 16; ++j) v[j] = 0.f;
         }
 #pragma unroll
-        for (int j = 0; j < 16; j += 4) *reinterpret_cast<float4*>(mine + c0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        for (int j = 0; j < 16; j += 4)
+          *reinterpret_cast<float4*>(mine + c0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
       }
       __threadfence();
       named_bar_sync(1, 128);
@@ -188,7 +301,8 @@ __global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_const
     }
 
     if (last) {
-      // Load columns [c0, c0+16) of this thread's row, summed over split-K slices.
+      // Columns [c0, c0+16) of this thread's row: split-K sum, times 1/rms of
+      // the token, plus bias (bias before any rounding, as in an HF linear).
       auto load_cols = [&](int c0, float* v) {
         if (args.splits > 1) {
 #pragma unroll
@@ -208,6 +322,20 @@ __global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_const
 #pragma unroll
           for (int j = 0; j < 16; ++j) v[j] = 0.f;
         }
+        if (args.rs_x != nullptr) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] *= args.swap ? rstd_s[c0 + j] : rs_row;
+        }
+        if (args.bias != nullptr) {
+          if (args.swap) {
+            const float b = m0 + r < args.M ? bf2f(args.bias[m0 + r]) : 0.f;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] += b;
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] += n0 + c0 + j < args.N ? bf2f(args.bias[n0 + c0 + j]) : 0.f;
+          }
+        }
       };
 
       if (args.epi == 0) {
@@ -223,9 +351,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_const
               for (int j = 0; j < 16; ++j) {
                 const int n = n0 + c0 + j;
                 if (n < args.N) {
-                  float y = v[j];
-                  if (args.bias) y += bf2f(args.bias[n]);
-                  y = rbf(y);
+                  float y = rbf(v[j]);
                   if (res) y += bf2f(res[n]);
                   o[n] = f2bf(y);
                 }
@@ -234,12 +360,11 @@ __global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_const
           } else {
             const int m = m0 + r;  // feature
             if (m < args.M) {
-              const float b = args.bias ? bf2f(args.bias[m]) : 0.f;
 #pragma unroll
               for (int j = 0; j < 16; ++j) {
                 const int t = n0 + c0 + j;  // token
                 if (t < args.N) {
-                  float y = rbf(v[j] + b);
+                  float y = rbf(v[j]);
                   if (args.residual) y += bf2f(args.residual[(size_t)t * args.ldr + m]);
                   args.out[(size_t)t * args.ldo + m] = f2bf(y);
                 }
@@ -247,7 +372,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_const
             }
           }
         }
-      } else if (!args.swap) {
+      } else if (args.epi == 1 && !args.swap) {
         // Normal SwiGLU: per 128-column block, gate = cols [0,64), up = [64,128).
         const int m = m0 + r;
         for (int blk = 0; blk < BN / 128; ++blk) {
@@ -268,14 +393,14 @@ __global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_const
             }
           }
         }
-      } else {
+      } else if (args.epi == 1) {
         // Swapped SwiGLU: tile rows [0,64) gate, [64,128) up of the same 64 features.
         for (int c0 = 0; c0 < BN; c0 += 16) {
           float v[16];
           load_cols(c0, v);
           if (r >= 64) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) xch[(r - 64) * (BN + 1) + c0 + j] = v[j];
+            for (int j = 0; j < 16; ++j) xch[(r - 64) * XCH_LD + j] = v[j];
           }
           named_bar_sync(1, 128);
           if (r < 64) {
@@ -285,7 +410,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_const
               for (int j = 0; j < 16; ++j) {
                 const int t = n0 + c0 + j;
                 if (t < args.N) {
-                  const float gg = rbf(v[j]), uu = rbf(xch[r * (BN + 1) + c0 + j]);
+                  const float gg = rbf(v[j]), uu = rbf(xch[r * XCH_LD + j]);
                   const float sg = rbf(gg / (1.f + __expf(-gg)));
                   args.out[(size_t)t * args.ldo + f] = f2bf(sg * uu);
                 }
@@ -293,6 +418,95 @@ __global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_const
             }
           }
           named_bar_sync(1, 128);
+        }
+      } else if (args.swap) {
+        // Swapped QKV: rows = 128 features (one D=128 head or two D=64 heads),
+        // columns = tokens.  Stage 16 tokens at a time, then one warp per token.
+        const int D = args.qkv.D;
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          float v[16];
+          load_cols(c0, v);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) xch[r * XCH_LD + j] = rbf(v[j]);
+          named_bar_sync(1, 128);
+          for (int j = ew; j < 16; j += 4) {
+            const int t = n0 + c0 + j;
+            if (t >= args.N) continue;
+            for (int hl = 0; hl < BM / D; ++hl) {
+              const int head = (m0 + hl * D) / D;
+              if (m0 + hl * D >= args.M) break;
+              if (D == 128) {
+                float hv[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) hv[i] = xch[(hl * D + lane * 4 + i) * XCH_LD + j];
+                qkv_head_store<4>(args.qkv, hv, head, t, lane);
+              } else {
+                float hv[2];
+#pragma unroll
+                for (int i = 0; i < 2; ++i) hv[i] = xch[(hl * D + lane * 2 + i) * XCH_LD + j];
+                qkv_head_store<2>(args.qkv, hv, head, t, lane);
+              }
+            }
+          }
+          named_bar_sync(1, 128);
+        }
+      } else {
+        // Normal QKV: this thread owns token row m and whole heads of the tile.
+        const int D = args.qkv.D;
+        const int m = m0 + r;
+        const QkvEpi& q = args.qkv;
+        for (int hl = 0; hl < BN / D; ++hl) {
+          const int col0 = hl * D;
+          if (n0 + col0 >= args.N) break;
+          const int head = (n0 + col0) / D;
+          const bool is_q = head < q.Hq, is_k = !is_q && head < q.Hq + q.Hkv;
+          const __nv_bfloat16* nw = is_q ? q.q_norm : (is_k ? q.k_norm : nullptr);
+          float hr = 1.f;
+          if (nw != nullptr) {
+            float ss = 0.f;
+            for (int c = 0; c < D; c += 16) {
+              float v[16];
+              load_cols(col0 + c, v);
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const float y = rbf(v[j]);
+                ss += y * y;
+              }
+            }
+            hr = rsqrtf(ss / D + q.eps);
+          }
+          if (m >= args.M) continue;
+          __nv_bfloat16* dst;
+          if (is_q) {
+            dst = q.q_out + ((size_t)m * q.Hq + head) * D;
+          } else {
+            const int slot = q.slots[m];
+            const int kh = is_k ? head - q.Hq : head - q.Hq - q.Hkv;
+            dst = q.kv + ((((size_t)(slot / q.PS)) * 2 + (is_k ? 0 : 1)) * q.Hkv + kh) * q.PS * (size_t)D +
+                  (size_t)(slot % q.PS) * D;
+          }
+          const int pos = q.positions[m];
+          for (int c = 0; c < D / 2; c += 16) {
+            float a[16], b[16];
+            load_cols(col0 + c, a);
+            load_cols(col0 + D / 2 + c, b);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              float x1 = rbf(a[j]), x2 = rbf(b[j]);
+              if (nw != nullptr) {
+                x1 = rbf(rbf(x1 * hr) * bf2f(nw[c + j]));
+                x2 = rbf(rbf(x2 * hr) * bf2f(nw[D / 2 + c + j]));
+              }
+              if (is_k && q.use_rope) {
+                const float cs = q.cos[(size_t)pos * (D / 2) + c + j], sn = q.sin[(size_t)pos * (D / 2) + c + j];
+                const float y1 = x1 * cs - x2 * sn, y2 = x2 * cs + x1 * sn;
+                x1 = y1;
+                x2 = y2;
+              }
+              dst[c + j] = f2bf(x1);
+              dst[D / 2 + c + j] = f2bf(x2);
+            }
+          }
         }
       }
     }
@@ -406,8 +620,7 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs&
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
     attr = true;
   }
-  kern<<<grid, 192, S::TOTAL, st>>>(ta, tb, a);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  launch_pdl(kern, grid, dim3(192), S::TOTAL, st, ta, tb, a);
 }
 
 static int num_sms() {
@@ -420,34 +633,31 @@ static int num_sms() {
   return n;
 }
 
-// out = x @ w^T (+bias) (+residual) ;  epi: 0 plain, 1 swiglu (w block-interleaved)
-void gemm(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
-          c10::optional<torch::Tensor> residual, int64_t epi) {
-  TORCH_CHECK(x.is_cuda() && w.is_cuda() && out.is_cuda(), "gemm: CUDA tensors required");
+static inline const __nv_bfloat16* opt_bf(const c10::optional<torch::Tensor>& t) {
+  return t.has_value() && t->defined() ? reinterpret_cast<const __nv_bfloat16*>(t->data_ptr()) : nullptr;
+}
+
+// Common driver: picks operand roles, tile width, split-K and launches.
+static void run_gemm(GemmArgs& a, const torch::Tensor& x, const torch::Tensor& w, bool fused_rms) {
+  TORCH_CHECK(x.is_cuda() && w.is_cuda(), "gemm: CUDA tensors required");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "gemm: bf16 only");
   TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1), "gemm: shape mismatch");
-  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && out.stride(1) == 1, "gemm: inner dim must be contiguous");
+  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1, "gemm: inner dim must be contiguous");
   const int T = x.size(0), K = x.size(1), F = w.size(0);
   TORCH_CHECK(K % 8 == 0 && x.stride(0) % 8 == 0 && w.stride(0) % 8 == 0, "gemm: K and strides must be multiples of 8");
   TORCH_CHECK((reinterpret_cast<uintptr_t>(x.data_ptr()) & 15) == 0 &&
               (reinterpret_cast<uintptr_t>(w.data_ptr()) & 15) == 0, "gemm: 16-byte aligned operands required");
-  if (epi == 1) TORCH_CHECK(F % 128 == 0, "gemm: swiglu weight rows must be a multiple of 128");
+  if (a.epi == 1) TORCH_CHECK(F % 128 == 0, "gemm: swiglu weight rows must be a multiple of 128");
   if (T == 0) return;
   const at::cuda::CUDAGuard guard(x.device());
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  GemmArgs a{};
   a.K = K;
-  a.epi = (int)epi;
-  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
-  a.ldo = out.stride(0);
-  a.bias = bias.has_value() && bias->defined() ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr;
-  a.residual = residual.has_value() && residual->defined() ? reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr()) : nullptr;
-  a.ldr = a.residual ? residual->stride(0) : 0;
+  a.rs_x = fused_rms ? reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()) : nullptr;
+  a.rs_ld = x.stride(0);
   const int kb_total = (K + BK - 1) / BK;
   const bool swap = T <= 64;
   a.swap = swap;
-  int BN;
-  int m_tiles, n_tiles;
+  int BN, m_tiles, n_tiles;
   if (swap) {
     BN = T <= 16 ? 16 : T <= 32 ? 32 : 64;
     a.M = F;
@@ -455,28 +665,27 @@ void gemm(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<tor
     m_tiles = (F + BM - 1) / BM;
     n_tiles = (T + BN - 1) / BN;
   } else {
-    BN = (F >= 4096 && T >= 512) ? 256 : 128;
+    BN = (F >= 4096 && T >= 512 && a.epi != 2) ? 256 : 128;
     a.M = T;
     a.N = F;
     m_tiles = (T + BM - 1) / BM;
     n_tiles = (F + BN - 1) / BN;
   }
   const int tiles = m_tiles * n_tiles;
-  // split-K so that the grid covers the machine (decode shapes have few tiles)
+  // Split-K so that one wave of resident CTAs (2 per SM for decode tiles)
+  // covers the machine; decode shapes have few output tiles.
   int splits = 1;
-  const int sms = num_sms();
-  if (tiles < sms) {
-    splits = std::max(1, std::min({(sms + tiles - 1) / tiles, kb_total / 4, 16}));
-  }
+  const int slots = num_sms() * (swap ? 2 : 1);
+  if (tiles < slots) splits = std::max(1, std::min({slots / tiles, kb_total / 2, 32}));
   int kbps = (kb_total + splits - 1) / splits;
   splits = (kb_total + kbps - 1) / kbps;
   a.splits = splits;
   a.kb_per_split = kbps;
-  int dev = x.get_device();
-  SplitKScratch& s = scratch_for(dev, splits > 1 ? (size_t)tiles * splits * BM * BN * 4 : 0, tiles);
-  a.ws = s.ws;
-  a.counters = s.counters;
-  a.err = s.err;
+  const int dev = x.get_device();
+  SplitKScratch& sc = scratch_for(dev, splits > 1 ? (size_t)tiles * splits * BM * BN * 4 : 0, tiles);
+  a.ws = sc.ws;
+  a.counters = sc.counters;
+  a.err = sc.err;
   dim3 grid(m_tiles, n_tiles, splits);
   const void* pa = swap ? w.data_ptr() : x.data_ptr();
   const void* pb = swap ? x.data_ptr() : w.data_ptr();
@@ -485,12 +694,60 @@ void gemm(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<tor
   CUtensorMap ta = make_tmap(pa, ra, K, lda, BM);
   CUtensorMap tb = make_tmap(pb, rb, K, ldb, BN);
   switch (BN) {
-    case 16: launch<16, 10>(ta, tb, a, grid, st); break;
-    case 32: launch<32, 10>(ta, tb, a, grid, st); break;
-    case 64: launch<64, 8>(ta, tb, a, grid, st); break;
+    case 16: launch<16, 4>(ta, tb, a, grid, st); break;
+    case 32: launch<32, 4>(ta, tb, a, grid, st); break;
+    case 64: launch<64, 4>(ta, tb, a, grid, st); break;
     case 128: launch<128, 6>(ta, tb, a, grid, st); break;
     default: launch<256, 4>(ta, tb, a, grid, st); break;
   }
+}
+
+// out = rms?(x) @ w^T (+bias) (+residual); epi: 0 plain, 1 swiglu (w block-interleaved).
+// rs_eps >= 0 enables the fused input RMSNorm (w must carry the folded norm weight).
+void gemm(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
+          c10::optional<torch::Tensor> residual, int64_t epi, double rs_eps) {
+  TORCH_CHECK(out.is_cuda() && out.stride(1) == 1, "gemm: out must be row-contiguous");
+  GemmArgs a{};
+  a.epi = (int)epi;
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.ldo = out.stride(0);
+  a.bias = opt_bf(bias);
+  a.residual = opt_bf(residual);
+  a.ldr = a.residual ? residual->stride(0) : 0;
+  a.rs_eps = (float)rs_eps;
+  run_gemm(a, x, w, rs_eps >= 0);
+}
+
+// qkv = rms?(x) @ w^T (+bias), then per-head q/k RMSNorm, RoPE(k) and the
+// paged KV append, all in the epilogue; q is written unrotated to q_out.
+void gemm_qkv(torch::Tensor q_out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
+              double rs_eps, torch::Tensor positions, torch::Tensor slots, torch::Tensor kv,
+              c10::optional<torch::Tensor> q_norm, c10::optional<torch::Tensor> k_norm, double head_eps,
+              torch::Tensor cos, torch::Tensor sin, int64_t Hq, int64_t Hkv, int64_t D, bool use_rope) {
+  TORCH_CHECK(D == 64 || D == 128, "gemm_qkv: head_dim must be 64 or 128");
+  TORCH_CHECK(w.size(0) == (Hq + 2 * Hkv) * D, "gemm_qkv: weight rows != (Hq + 2 Hkv) * D");
+  TORCH_CHECK(kv.is_contiguous() && kv.size(2) == Hkv && kv.size(4) == D, "gemm_qkv: cache layout");
+  TORCH_CHECK(positions.scalar_type() == at::kInt && slots.scalar_type() == at::kInt, "gemm_qkv: int32 metadata");
+  GemmArgs a{};
+  a.epi = 2;
+  a.bias = opt_bf(bias);
+  a.rs_eps = (float)rs_eps;
+  QkvEpi& q = a.qkv;
+  q.q_out = reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr());
+  q.kv = reinterpret_cast<__nv_bfloat16*>(kv.data_ptr());
+  q.slots = slots.data_ptr<int>();
+  q.positions = positions.data_ptr<int>();
+  q.q_norm = opt_bf(q_norm);
+  q.k_norm = opt_bf(k_norm);
+  q.cos = cos.data_ptr<float>();
+  q.sin = sin.data_ptr<float>();
+  q.Hq = Hq;
+  q.Hkv = Hkv;
+  q.D = D;
+  q.PS = kv.size(3);
+  q.use_rope = use_rope ? 1 : 0;
+  q.eps = (float)head_eps;
+  run_gemm(a, x, w, rs_eps >= 0);
 }
 
 int64_t gemm_check_error(int64_t device) {

@@ -26,7 +26,7 @@ def test_gemm_plain(M, N, K):
     x = torch.randn(M, K, device=DEV, generator=g).bfloat16()
     w = (torch.randn(N, K, device=DEV, generator=g) * 0.05).bfloat16()
     out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
-    _ext().gemm(out, x, w, None, None, 0)
+    _ext().gemm(out, x, w, None, None, 0, -1.0)
     torch.cuda.synchronize()
     _check_err()
     ref = x.float() @ w.float().t()
@@ -40,12 +40,12 @@ def test_gemm_bias_residual(M, N, K):
     b = torch.randn(N, device=DEV).bfloat16()
     r = torch.randn(M, N, device=DEV).bfloat16()
     out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
-    _ext().gemm(out, x, w, b, r, 0)
+    _ext().gemm(out, x, w, b, r, 0, -1.0)
     ref = (x.float() @ w.float().t() + b.float()).bfloat16().float() + r.float()
     torch.testing.assert_close(out.float(), ref, atol=5e-2, rtol=2e-2)
     # in place residual update (out aliases the residual)
     r2 = r.clone()
-    _ext().gemm(r2, x, w, b, r2, 0)
+    _ext().gemm(r2, x, w, b, r2, 0, -1.0)
     torch.testing.assert_close(r2.float(), ref, atol=5e-2, rtol=2e-2)
 
 
@@ -53,15 +53,56 @@ def test_gemm_bias_residual(M, N, K):
 def test_gemm_swiglu(M, I, K):
     from braidinfer_b200.ops.linear import interleave_gate_up, swiglu_ref_from_interleaved
     x = torch.randn(M, K, device=DEV).bfloat16()
+    _check_err()
     wg = (torch.randn(I, K, device=DEV) * 0.05).bfloat16()
     wu = (torch.randn(I, K, device=DEV) * 0.05).bfloat16()
     w = interleave_gate_up(wg, wu)
     out = torch.empty(M, w.shape[0] // 2, device=DEV, dtype=torch.bfloat16)
-    _ext().gemm(out, x, w, None, None, 1)
+    _ext().gemm(out, x, w, None, None, 1, -1.0)
     ref = swiglu_ref_from_interleaved(x.float() @ w.float().t(), torch.bfloat16)
     torch.testing.assert_close(out.float(), ref.float(), atol=3e-2, rtol=3e-2)
     direct = torch.nn.functional.silu(x.float() @ wg.float().t()) * (x.float() @ wu.float().t())
     torch.testing.assert_close(out.float()[:, :I], direct, atol=5e-2, rtol=5e-2)
+
+
+@pytest.mark.parametrize("M,N,K", [(5, 1024, 2048), (64, 512, 4096), (300, 768, 1024)])
+def test_gemm_fused_rmsnorm(M, N, K):
+    """rms(x) @ (W diag(g))^T == (x / rms(x) * g) @ W^T"""
+    from braidinfer_b200 import ops
+    x = (torch.randn(M, K, device=DEV) * 3).bfloat16()
+    w = (torch.randn(N, K, device=DEV) * 0.05).bfloat16()
+    g = (torch.rand(K, device=DEV) + 0.5).bfloat16()
+    wf = (w.float() * g.float()).bfloat16()
+    out = ops.linear(x, wf, rms_eps=1e-5)
+    xn = x.float() * torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + 1e-5) * g.float()
+    torch.testing.assert_close(out.float(), xn @ w.float().t(), atol=5e-2, rtol=3e-2)
+    sw = ops.linear_swiglu(x, torch.cat([wf[:128], wf[:128]])[:256].contiguous(), rms_eps=1e-5)
+    assert sw.shape == (M, 128) and torch.isfinite(sw.float()).all()
+
+
+@pytest.mark.parametrize("T,D,Hq,Hkv,qk_norm,bias", [(3, 128, 16, 8, True, False), (40, 64, 32, 4, False, True),
+                                                      (200, 128, 8, 2, True, True), (1, 64, 4, 2, False, False)])
+def test_gemm_qkv_epilogue(T, D, Hq, Hkv, qk_norm, bias):
+    """Fused QKV GEMM epilogue == linear + qkv_prepare (both native), and the CPU path."""
+    from braidinfer_b200 import ops
+    H, PS, P = 512, 16, 64
+    x = torch.randn(T, H, device=DEV).bfloat16()
+    w = (torch.randn((Hq + 2 * Hkv) * D, H, device=DEV) * 0.05).bfloat16()
+    b = (torch.randn((Hq + 2 * Hkv) * D, device=DEV) * 0.1).bfloat16() if bias else None
+    pos = torch.randint(0, 900, (T,), device=DEV, dtype=torch.int32)
+    slots = torch.randperm(P * PS, device=DEV)[:T].int()
+    cos, sin = ops.build_cos_sin(D, 10000.0, 1024, device=DEV)
+    qn = (torch.rand(D, device=DEV) * 2).bfloat16() if qk_norm else None
+    kn = (torch.rand(D, device=DEV) * 80 - 40).bfloat16() if qk_norm else None
+    kv1 = torch.zeros(P, 2, Hkv, PS, D, device=DEV, dtype=torch.bfloat16)
+    kv2 = kv1.clone()
+    q1 = ops.qkv_gemm(x, w, b, 1e-6, pos, slots, kv1, Hq, Hkv, D, cos, sin, qn, kn, 1e-6, True)
+    qkv = ops.linear(x, w, b, rms_eps=1e-6)
+    q2 = ops.qkv_prepare(qkv, pos, slots, kv2, Hq, Hkv, D, cos, sin, qn, kn, 1e-6, True)
+    tol = 0.05 * (40 if qk_norm else 1)
+    torch.testing.assert_close(q1.float(), q2.float(), atol=tol, rtol=3e-2)
+    torch.testing.assert_close(kv1.float(), kv2.float(), atol=tol, rtol=3e-2)
+    _check_err()
 
 
 def test_rmsnorm_and_add():
