@@ -759,3 +759,137 @@ int64_t gemm_check_error(int64_t device) {
 }
 
 }  // namespace braid
+
+// ===================================================================
+// Allocation-free entry point (declared and documented in gemm_noalloc.h).
+// ===================================================================
+#include "gemm_noalloc.h"
+
+namespace braid {
+namespace noalloc {
+
+struct Scratch {
+  float partial[BRAID_NOALLOC_PARTIAL_BYTES / sizeof(float)];
+  int counters[BRAID_NOALLOC_MAX_TILES];
+  int err;
+};
+// One fixed scratch per device for the whole process lifetime.
+static __device__ __align__(256) Scratch g_scratch;
+
+constexpr int kMaxDevices = 64;
+static Scratch* g_addr[kMaxDevices] = {};
+static std::mutex g_setup_mu;
+static thread_local char g_msg[256] = "";
+
+static int fail(int code, const char* what) {
+  snprintf(g_msg, sizeof(g_msg), "braid_gemm_noalloc: %s", what);
+  return code;
+}
+
+static CUtensorMap encode(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows, bool* ok) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = get_encode()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
+                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  *ok = r == CUDA_SUCCESS;
+  return m;
+}
+
+template <int BN>
+static cudaError_t launch_plain(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, dim3 grid,
+                                cudaStream_t st) {
+  using S = GemmSmem<BN, 4>;
+  auto kern = gemm_tcgen05_kernel<BN, 4>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL);
+  if (e != cudaSuccess) return e;
+  kern<<<grid, 192, S::TOTAL, st>>>(ta, tb, a);
+  return cudaGetLastError();
+}
+
+}  // namespace noalloc
+}  // namespace braid
+
+extern "C" const char* braid_gemm_noalloc_last_error(void) { return braid::noalloc::g_msg; }
+
+extern "C" int braid_gemm_noalloc(void* out, const void* x, const void* w, const void* bias, const void* residual,
+                                  int T, int N, int K, int ldo, int ldx, int ldw, int ldr, float rs_eps,
+                                  void* stream) {
+  using namespace braid;
+  using namespace braid::noalloc;
+  g_msg[0] = 0;
+  if (out == nullptr || x == nullptr || w == nullptr) return fail(1, "null operand");
+  if (T < 1 || T > BRAID_NOALLOC_MAX_TOKENS) return fail(2, "T must be in [1, 64] (decode shapes only)");
+  if (N < 1 || K < 8 || K % 8 || ldx % 8 || ldw % 8 || ldx < K || ldw < K || ldo < N)
+    return fail(3, "K and the row strides must be multiples of 8 and at least the row length");
+  if (((uintptr_t)x | (uintptr_t)w) & 15) return fail(4, "x and w must be 16-byte aligned");
+  if (residual != nullptr && ldr < N) return fail(3, "residual stride shorter than N");
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return fail(5, "no current CUDA device");
+  Scratch* sc = g_addr[dev];
+  if (sc == nullptr) {
+    // Set-up on this device (it is current): resolve the array's device address.
+    std::lock_guard<std::mutex> g(g_setup_mu);
+    if (g_addr[dev] == nullptr) {
+      void* p = nullptr;
+      cudaError_t e = cudaGetSymbolAddress(&p, g_scratch);
+      if (e != cudaSuccess || p == nullptr) return fail(6, cudaGetErrorString(e));
+      e = cudaMemset(p, 0, sizeof(Scratch));
+      if (e != cudaSuccess) return fail(6, cudaGetErrorString(e));
+      g_addr[dev] = static_cast<Scratch*>(p);
+    }
+    sc = g_addr[dev];
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  GemmArgs a{};
+  a.K = K;
+  a.swap = 1;
+  a.epi = 0;
+  a.M = N;
+  a.N = T;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.ldo = ldo;
+  a.bias = static_cast<const __nv_bfloat16*>(bias);
+  a.residual = static_cast<const __nv_bfloat16*>(residual);
+  a.ldr = ldr;
+  a.rs_x = rs_eps >= 0.f ? static_cast<const __nv_bfloat16*>(x) : nullptr;
+  a.rs_ld = ldx;
+  a.rs_eps = rs_eps;
+  const int BN = T <= 16 ? 16 : T <= 32 ? 32 : 64;
+  const int m_tiles = (N + BM - 1) / BM;
+  const int tiles = m_tiles;
+  const int kb_total = (K + BK - 1) / BK;
+  int splits = 1;
+  const int slots = num_sms() * 2;
+  if (tiles < slots) splits = std::max(1, std::min({slots / tiles, kb_total / 2, 32}));
+  // never more scratch than the fixed array holds
+  while (splits > 1 && ((size_t)tiles * splits * BM * BN * 4 > BRAID_NOALLOC_PARTIAL_BYTES || tiles > BRAID_NOALLOC_MAX_TILES))
+    --splits;
+  int kbps = (kb_total + splits - 1) / splits;
+  splits = (kb_total + kbps - 1) / kbps;
+  a.splits = splits;
+  a.kb_per_split = kbps;
+  a.ws = sc->partial;
+  a.counters = sc->counters;
+  a.err = &sc->err;
+  // counters and the error word must start at zero for this call
+  if (cudaMemsetAsync(sc->counters, 0, sizeof(int) * (splits > 1 ? tiles : 1), st) != cudaSuccess ||
+      cudaMemsetAsync(&sc->err, 0, sizeof(int), st) != cudaSuccess)
+    return fail(7, "clearing the scratch counters failed");
+  bool ok1 = false, ok2 = false;
+  CUtensorMap ta = encode(w, N, K, ldw, BM, &ok1);
+  CUtensorMap tb = encode(x, T, K, ldx, BN, &ok2);
+  if (!ok1 || !ok2) return fail(8, "tensor map encoding failed");
+  dim3 grid(m_tiles, 1, splits);
+  cudaError_t e;
+  switch (BN) {
+    case 16: e = launch_plain<16>(ta, tb, a, grid, st); break;
+    case 32: e = launch_plain<32>(ta, tb, a, grid, st); break;
+    default: e = launch_plain<64>(ta, tb, a, grid, st); break;
+  }
+  if (e != cudaSuccess) return fail(9, cudaGetErrorString(e));
+  return 0;
+}
