@@ -56,7 +56,7 @@ class _GraphSlot:
         self.page_cap = 0
         self.num_splits = 1
         self.launches = 0
-        self.pin_meta = self.pin_f = self.pin_k = self.pin_l = self.pin_out = None
+        self.pin_meta = self.pin_f = self.pin_k = self.pin_l = self.pin_out = self.pin_status = None
 
 
 class ModelRunner:
@@ -84,6 +84,7 @@ class ModelRunner:
         self.timing = {"steps": 0, "prefill_tokens": 0, "decode_tokens": 0}
         self.capture_logits: Optional[list] = None  # debug/test hook (eager steps only)
         self.event_log: Optional[list] = None  # (start, end) CUDA events around each graph replay
+        self.fused_comm = None  # set when the peer-memory TP runtime is enabled
         self.last_h2d_bytes = 0
 
     # ------------------------------------------------------------- KV pool
@@ -207,6 +208,8 @@ class ModelRunner:
         order = with_tokens + empty
         hn = torch.cat(rows) if len(rows) > 1 else rows[0]
         toks = self.sample(hn, order).tolist()
+        if self.fused_comm is not None:
+            self.fused_comm.check()
         by_id = {s.seq_id: t for s, t in zip(order, toks)}
         return [by_id[s.seq_id] for s in seqs]
 
@@ -340,7 +343,13 @@ class ModelRunner:
         else:
             g.graph.replay()
         g.pin_out.copy_(g.out, non_blocking=True)
+        if self.fused_comm is not None:
+            if g.pin_status is None:
+                g.pin_status = torch.zeros(4, dtype=torch.int32).pin_memory()
+            g.pin_status.copy_(self.fused_comm.status, non_blocking=True)
         torch.cuda.current_stream(self.device).synchronize()
+        if self.fused_comm is not None and int(g.pin_status[0]) != 0:
+            self.fused_comm.check()
         return g.pin_out[: len(seqs)].tolist()
 
     def launches_per_decode_step(self, batch: int) -> int:

@@ -81,9 +81,11 @@ class DecoderLM:
             w.gu_w = torch.zeros(2 * L.inter_pad, H, **kw)
             w.down_w = torch.zeros(H, L.inter_pad, **kw)
             self.layers.append(w)
-        self.embed = torch.empty(L.vocab_local, H, **kw)
+        # The input embedding is replicated on every rank (a gather needs no
+        # collective); the LM head is vocab-parallel (rows [vocab_start, +local)).
+        self.embed = torch.empty(spec.vocab_size, H, **kw)
         self.final_norm = torch.ones(H, **kw)
-        self.lm_head = self.embed if spec.tie_word_embeddings else torch.empty(L.vocab_local, H, **kw)
+        self.lm_head = None if spec.tie_word_embeddings else torch.empty(L.vocab_local, H, **kw)
         self.lm_head_folded = None  # lm_head * final_norm, built by finalize()
         self.finalized = False
         # RoPE tables: room for query positions shifted by chunk deltas.
@@ -121,8 +123,14 @@ class DecoderLM:
             fill(w.down_w[:, :L.inter])
             if k_norm_range is not None and w.k_norm is not None:
                 w.k_norm.uniform_(-k_norm_range, k_norm_range, generator=g)
-        fill(self.embed)
-        if self.lm_head is not self.embed:
+        if self.tp.size > 1:
+            # identical replicated table on every rank
+            ge = torch.Generator(device=self.device)
+            ge.manual_seed(seed + 104729)
+            self.embed.normal_(0.0, std, generator=ge)
+        else:
+            fill(self.embed)
+        if self.lm_head is not None:
             fill(self.lm_head)
 
     # --------------------------------------------------------------- loading
@@ -132,10 +140,10 @@ class DecoderLM:
         D = S.head_dim
         t = t.to(self.dtype)
         if name in ("model.embed_tokens.weight", "embed_tokens.weight"):
-            self.embed.copy_(t[L.vocab_start:L.vocab_start + L.vocab_local])
+            self.embed.copy_(t)
             return True
         if name in ("lm_head.weight",):
-            if self.lm_head is self.embed:
+            if self.lm_head is None:
                 return True
             self.lm_head.copy_(t[L.vocab_start:L.vocab_start + L.vocab_local])
             return True
@@ -214,15 +222,17 @@ class DecoderLM:
         for w in self.layers:
             fold(w.qkv_w, w.in_norm)
             fold(w.gu_w, w.post_norm)
-        self.lm_head_folded = (self.lm_head.float() * self.final_norm.float()[None, :]).to(self.dtype)
+        L = self.layout
+        head = self.lm_head if self.lm_head is not None else self.embed[L.vocab_start:L.vocab_start + L.vocab_local]
+        folded = (head.float() * self.final_norm.float()[None, :]).to(self.dtype)
+        if folded.shape[0] < L.vocab_per_rank:  # equal shards for the logits all-gather
+            folded = torch.cat([folded, folded.new_zeros(L.vocab_per_rank - folded.shape[0], folded.shape[1])])
+        self.lm_head_folded = folded.contiguous()
         self.finalized = True
 
     # --------------------------------------------------------------- forward
     def embed_tokens(self, input_ids: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
-        h = ops.embedding(input_ids, self.embed, self.layout.vocab_start)
-        if self.tp.size > 1:
-            h = comm.all_reduce(h)
-        return h
+        return ops.embedding(input_ids, self.embed, 0)
 
     def forward(self, input_ids: torch.Tensor, positions: torch.Tensor, slot_mapping: torch.Tensor,
                 meta, kv_cache: torch.Tensor, workspace: Optional[Dict] = None) -> torch.Tensor:
@@ -235,16 +245,19 @@ class DecoderLM:
             q = ops.qkv_gemm(residual, w.qkv_w, w.qkv_b, eps, positions, slot_mapping, kv_cache[i], L.q_heads,
                              L.kv_heads, S.head_dim, self.cos, self.sin, w.q_norm, w.k_norm, eps, S.use_rope)
             o = ops.attention(q, kv_cache[i], meta, self.cos, self.sin, self.scale, S.use_rope, workspace)
-            if self.tp.size == 1:
-                residual = ops.linear(o, w.o_w, residual=residual, out=residual)
-            else:
-                residual = comm.all_reduce_add(ops.linear(o, w.o_w), residual)
+            residual = self._row_parallel(o, w.o_w, residual)
             g = ops.linear_swiglu(residual, w.gu_w, rms_eps=eps)
-            if self.tp.size == 1:
-                residual = ops.linear(g, w.down_w, residual=residual, out=residual)
-            else:
-                residual = comm.all_reduce_add(ops.linear(g, w.down_w), residual)
+            residual = self._row_parallel(g, w.down_w, residual)
         return residual
+
+    def _row_parallel(self, x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor) -> torch.Tensor:
+        """``residual += x @ w.T`` summed over tensor-parallel ranks."""
+        if self.tp.size == 1:
+            return ops.linear(x, w, residual=residual, out=residual)
+        fc = comm.get_fused_comm()
+        if fc is not None and fc.can_all_reduce(residual):
+            return fc.linear_all_reduce_add(x, w, residual)
+        return comm.all_reduce_add(ops.linear(x, w), residual)
 
     def final_hidden(self, h: torch.Tensor) -> torch.Tensor:
         """Rows fed to the LM head; the final RMSNorm is fused into ``compute_logits``."""

@@ -64,9 +64,11 @@ def all_gather_last(x: torch.Tensor, full: Optional[int] = None) -> torch.Tensor
     tp = get_tp()
     if tp.size == 1:
         return x
-    parts = [torch.empty_like(x) for _ in range(tp.size)]
-    dist.all_gather(parts, x.contiguous(), group=tp.group)
-    y = torch.cat(parts, dim=-1)
+    x = x.contiguous()
+    g = torch.empty((tp.size * x.shape[0],) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
+    dist.all_gather_into_tensor(g, x, group=tp.group)
+    g = g.view((tp.size,) + tuple(x.shape))
+    y = g.movedim(0, -2).reshape(*x.shape[:-1], tp.size * x.shape[-1])
     return y[..., :full] if full is not None else y
 
 

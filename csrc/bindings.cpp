@@ -9,6 +9,17 @@ void gemm_qkv(torch::Tensor q_out, torch::Tensor x, torch::Tensor w, c10::option
               c10::optional<torch::Tensor> q_norm, c10::optional<torch::Tensor> k_norm, double head_eps,
               torch::Tensor cos, torch::Tensor sin, int64_t Hq, int64_t Hkv, int64_t D, bool use_rope);
 int64_t gemm_check_error(int64_t device);
+int64_t gemm_push(torch::Tensor x, torch::Tensor w, torch::Tensor peers, int64_t flags_off, int64_t rank, int64_t tp,
+                  int64_t maxT, torch::Tensor epoch_state);
+std::vector<torch::Tensor> comm_alloc(int64_t nbytes, int64_t device);
+int64_t comm_open(torch::Tensor handle, int64_t device);
+void comm_close(int64_t ptr, int64_t device);
+void comm_free(int64_t ptr, int64_t device);
+void tp_push(torch::Tensor x, torch::Tensor peers, int64_t flags_off, int64_t rank, int64_t tp, int64_t maxT,
+             torch::Tensor epoch_state);
+void tp_reduce_add(torch::Tensor out, torch::Tensor residual, bool add_residual, int64_t buf, int64_t flags_off,
+                   int64_t tp, int64_t maxT, int64_t rank, int64_t arrivals_per_call, torch::Tensor epoch_state,
+                   torch::Tensor status, double timeout_s);
 void attention(torch::Tensor out, torch::Tensor q, torch::Tensor kv, torch::Tensor qo_indptr,
                torch::Tensor positions, torch::Tensor seg_indptr, torch::Tensor seg_page_indptr,
                torch::Tensor seg_offset, torch::Tensor seg_len, torch::Tensor seg_pos0, torch::Tensor seg_delta,
@@ -32,6 +43,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "braidinfer_b200 native sm_100a kernels";
   m.def("gemm", &braid::gemm, "tcgen05 GEMM out = x @ w^T (+bias)(+residual); epi 1 = SwiGLU");
   m.def("gemm_qkv", &braid::gemm_qkv, "tcgen05 QKV GEMM with fused q/k-norm, RoPE(k) and paged KV append");
+  m.def("gemm_push", &braid::gemm_push, "row-parallel GEMM whose epilogue pushes bf16 tiles to TP peers");
+  m.def("comm_alloc", &braid::comm_alloc, "cudaMalloc a comm buffer; returns (ptr, ipc handle)");
+  m.def("comm_open", &braid::comm_open, "map a peer's comm buffer from its IPC handle");
+  m.def("comm_close", &braid::comm_close);
+  m.def("comm_free", &braid::comm_free);
+  m.def("tp_push", &braid::tp_push, "push a bf16 partial to every TP peer");
+  m.def("tp_reduce_add", &braid::tp_reduce_add, "bounded-wait sum of pushed partials (+ residual)");
   m.def("gemm_check_error", &braid::gemm_check_error, "read and clear the GEMM bounded-wait error flag");
   m.def("attention", &braid::attention, "paged cascade attention (decode/prefill)");
   m.def("rms_norm", &braid::rms_norm);

@@ -54,10 +54,21 @@ struct QkvEpi {
   float eps;
 };
 
+// Push epilogue (epi == 3, swapped mode): the bf16 result tile is written to
+// every tensor-parallel peer's receive area (slot epoch & 1, source row rank)
+// instead of local memory, then each peer's arrival counter for this rank is
+// bumped; tp_reduce_add in comm.cu completes the all-reduce.
+struct PushEpi {
+  const uint64_t* peers;       // [tp] base addresses of the peers' comm buffers
+  int64_t flags_off;           // byte offset of the arrival counters in a comm buffer
+  const uint64_t* epoch_state; // local epoch (completed all-reduce calls)
+  int rank, tp, maxT;
+};
+
 struct GemmArgs {
   int M, N, K;        // A rows, B rows, reduction length
   int swap;           // 1: A is the weight, output written transposed
-  int epi;            // 0 plain, 1 swiglu, 2 qkv
+  int epi;            // 0 plain, 1 swiglu, 2 qkv, 3 push
   __nv_bfloat16* out;
   int ldo;
   const __nv_bfloat16* bias;      // indexed by feature
@@ -74,6 +85,7 @@ struct GemmArgs {
   int* counters;      // one per output tile, kept at zero between launches
   int* err;           // error flag (bounded-wait timeout)
   QkvEpi qkv;
+  PushEpi push;
 };
 
 constexpr int BM = 128;
@@ -371,6 +383,34 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
               }
             }
           }
+        }
+      } else if (args.epi == 3) {
+        // Push: result tile -> every peer's receive slot, then arrival counters.
+        const PushEpi& ps = args.push;
+        const int slot = (int)(ps.epoch_state[0] & 1);
+        const int m = m0 + r;  // feature (swapped mode)
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          float v[16];
+          load_cols(c0, v);
+          if (m < args.M) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int t = n0 + c0 + j;
+              if (t < args.N) {
+                const __nv_bfloat16 y = f2bf(v[j]);
+                for (int p = 0; p < ps.tp; ++p)
+                  reinterpret_cast<__nv_bfloat16*>(ps.peers[p])[(((size_t)slot * ps.tp + ps.rank) * ps.maxT + t) *
+                                                                    args.M + m] = y;
+              }
+            }
+          }
+        }
+        __threadfence_system();
+        named_bar_sync(1, 128);
+        if (et == 0) {
+          for (int p = 0; p < ps.tp; ++p)
+            atomicAdd(reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(ps.peers[p]) + ps.flags_off) +
+                          ps.rank, 1ull);
         }
       } else if (args.epi == 1 && !args.swap) {
         // Normal SwiGLU: per 128-column block, gate = cols [0,64), up = [64,128).
@@ -758,6 +798,28 @@ int64_t gemm_check_error(int64_t device) {
   return h;
 }
 
+}  // namespace braid
+
+namespace braid {
+// Row-parallel GEMM whose epilogue pushes the result to every tensor-parallel
+// peer (decode shapes).  Returns the number of tiles pushed, i.e. the arrivals
+// each peer must count from this rank for this call.
+int64_t gemm_push(torch::Tensor x, torch::Tensor w, torch::Tensor peers, int64_t flags_off, int64_t rank, int64_t tp,
+                  int64_t maxT, torch::Tensor epoch_state) {
+  TORCH_CHECK(x.size(0) <= 64 && x.size(0) <= maxT, "gemm_push: decode shapes only (<= 64 tokens)");
+  GemmArgs a{};
+  a.epi = 3;
+  a.push.peers = reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>());
+  a.push.flags_off = flags_off;
+  a.push.epoch_state = reinterpret_cast<const uint64_t*>(epoch_state.data_ptr<int64_t>());
+  a.push.rank = rank;
+  a.push.tp = tp;
+  a.push.maxT = maxT;
+  run_gemm(a, x, w, false);
+  const int T = x.size(0), F = w.size(0);
+  const int BN = T <= 16 ? 16 : T <= 32 ? 32 : 64;
+  return (int64_t)((F + BM - 1) / BM) * ((T + BN - 1) / BN);
+}
 }  // namespace braid
 
 // ===================================================================

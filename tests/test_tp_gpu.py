@@ -1,0 +1,177 @@
+"""Tensor parallelism on 2 GPUs (child processes, one per GPU, NCCL with NVLS
+off; our kernels use plain peer stores, never multimem).
+
+* the fused peer-memory all-reduce equals NCCL's;
+* a TP2 engine (fused and NCCL backends) matches TP1 logits;
+* a peer that never signals makes the bounded wait expire: both ranks get
+  CommTimeoutError and the CUDA context stays usable.
+"""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+needs2 = pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                            reason="needs 2 GPUs")
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _env(rank, world, port):
+    os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank), MASTER_ADDR="127.0.0.1",
+                      MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+
+
+def _w_allreduce(rank, world, port, q):
+    _env(rank, world, port)
+    import datetime
+    import torch.distributed as dist
+    try:
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+        from braidinfer_b200.parallel.state import init_tp
+        from braidinfer_b200.parallel.symm import FusedComm
+        tp = init_tp(world)
+        fc = FusedComm(tp, 1024, torch.device("cuda", rank), max_tokens=16, timeout_s=5.0)
+        errs = []
+        for it in range(6):
+            g = torch.Generator(device="cuda").manual_seed(100 * it + rank)
+            x = torch.randn(7 + it, 1024, device="cuda", generator=g).bfloat16()
+            res = torch.randn(7 + it, 1024, device="cuda", generator=torch.Generator(device="cuda").manual_seed(it)).bfloat16()
+            ref = x.float().clone()
+            dist.all_reduce(ref)
+            ref = (res.float() + ref.bfloat16().float())
+            out = fc.all_reduce_add(x, res.clone())
+            torch.cuda.synchronize()
+            fc.check()
+            errs.append((out.float() - ref).abs().max().item())
+        # GEMM with the push fused into its epilogue
+        xw = torch.randn(5, 512, device="cuda").bfloat16()
+        w = (torch.randn(1024, 512, device="cuda", generator=torch.Generator(device="cuda").manual_seed(rank)) * 0.05).bfloat16()
+        part = (xw.float() @ w.float().t()).bfloat16()
+        ref = part.float().clone()
+        dist.all_reduce(ref)
+        res = torch.zeros(5, 1024, device="cuda", dtype=torch.bfloat16)
+        out = fc.linear_all_reduce_add(xw, w, res)
+        torch.cuda.synchronize()
+        fc.check()
+        errs.append((out.float() - ref).abs().max().item())
+        q.put((rank, errs))
+        fc.close()
+    except Exception:
+        import traceback
+        q.put((rank, traceback.format_exc()))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def _w_timeout(rank, world, port, q):
+    _env(rank, world, port)
+    import datetime
+    import time
+    import torch.distributed as dist
+    try:
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+        from braidinfer_b200.errors import CommTimeoutError
+        from braidinfer_b200.parallel.state import init_tp
+        from braidinfer_b200.parallel.symm import FusedComm
+        tp = init_tp(world)
+        fc = FusedComm(tp, 256, torch.device("cuda", rank), max_tokens=8, timeout_s=0.5)
+        fc.push_fault = rank == 0  # rank 0 never signals its arrival
+        x = torch.ones(4, 256, device="cuda", dtype=torch.bfloat16)
+        t0 = time.time()
+        raised = False
+        try:
+            fc.all_reduce(x)
+            torch.cuda.synchronize()
+            fc.check()
+        except CommTimeoutError as e:
+            raised = e.status.get("peer") == 0
+        dt = time.time() - t0
+        y = (torch.arange(10, device="cuda") * 2).sum().item()  # context still usable
+        q.put((rank, raised, dt, y))
+    except Exception:
+        import traceback
+        q.put((rank, traceback.format_exc(), 0, 0))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def _w_engine(rank, world, port, ckpt, backend, q):
+    _env(rank, world, port)
+    import torch.distributed as dist
+    try:
+        from braidinfer_b200 import LLM, SamplingParams
+        llm = LLM(ckpt, num_kvcache_blocks=32, kvcache_block_size=16, tensor_parallel_size=world,
+                  comm_backend=backend, max_graph_batch=4)
+        llm.model_runner.capture_logits = []
+        out = llm.generate([list(range(3, 60)), list(range(5, 20))],
+                           SamplingParams(temperature=0, max_tokens=6, ignore_eos=True))
+        lg = llm.model_runner.capture_logits[0].numpy()
+        q.put((rank, [o["token_ids"] for o in out], lg))
+        llm.exit()
+    except Exception:
+        import traceback
+        q.put((rank, traceback.format_exc(), None))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def _spawn(fn, world, *args):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=fn, args=(r, world, port) + args + (q,)) for r in range(world)]
+    [p.start() for p in ps]
+    out = [q.get(timeout=600) for _ in ps]
+    [p.join(timeout=120) for p in ps]
+    return sorted(out, key=lambda r: r[0])
+
+
+@needs2
+def test_fused_all_reduce_matches_nccl():
+    for r in _spawn(_w_allreduce, 2):
+        assert isinstance(r[1], list), r[1]
+        assert max(r[1]) < 0.05, r[1]
+
+
+@needs2
+def test_peer_never_signals_times_out():
+    res = _spawn(_w_timeout, 2)
+    for r in res:
+        assert r[1] is True or r[1] is False, r[1]
+        assert r[1], f"rank {r[0]} did not raise CommTimeoutError"
+        assert r[2] < 20
+        assert r[3] == 90
+
+
+@needs2
+@pytest.mark.parametrize("backend", ["fused", "nccl"])
+def test_tp2_engine_matches_tp1(tmp_path, backend):
+    from braidinfer_b200 import LLM, SamplingParams
+    from braidinfer_b200.utils.synthetic import make_checkpoint
+    ckpt = make_checkpoint(str(tmp_path / "m"), "tiny-llama", seed=3, dtype=torch.bfloat16)
+    llm = LLM(ckpt, num_kvcache_blocks=32, kvcache_block_size=16, max_graph_batch=4)
+    llm.model_runner.capture_logits = []
+    llm.generate([list(range(3, 60)), list(range(5, 20))], SamplingParams(temperature=0, max_tokens=6, ignore_eos=True))
+    ref = llm.model_runner.capture_logits[0].numpy()
+    del llm
+    res = _spawn(_w_engine, 2, ckpt, backend)
+    for r in res:
+        assert r[2] is not None, r[1]
+        d = abs(r[2] - ref).max()
+        assert d < 0.05 * abs(ref).max() + 0.05, d
