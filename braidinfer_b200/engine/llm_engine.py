@@ -83,6 +83,12 @@ class LLMEngine:
             unk = self.tokenizer.unk_token_id
             if all(i is not None and i != unk for i in ids):
                 self.think_token_ids = tuple(ids)
+        self._heartbeat = None
+        self._steps = 0
+        if tp.size > 1 and config.heartbeat_every > 0:
+            from ..parallel.health import Heartbeat
+
+            self._heartbeat = Heartbeat(timeout_s=max(1.0, config.comm_timeout_s))
         if config.use_cuda_graphs:
             self.model_runner.capture_all(min(config.max_graph_batch, config.max_num_seqs))
         self._closed = False
@@ -143,6 +149,9 @@ class LLMEngine:
 
     # --------------------------------------------------------------- step
     def step(self) -> List[Sequence]:
+        self._steps += 1
+        if self._heartbeat is not None and self._steps % self.config.heartbeat_every == 0:
+            self._heartbeat.check(self._steps)  # PeerFailureError before any collective of this step
         seqs, is_prefill = self.scheduler.schedule()
         if not seqs:
             return []
