@@ -31,6 +31,7 @@
 
 #include "common.cuh"
 #include "launch.cuh"
+#include "tmap.h"
 
 #include <mutex>
 #include <unordered_map>
@@ -60,6 +61,7 @@ struct AttnParams {
   float* part_o;    // [T, Hq, splits, D]
   float* part_lse;  // [T, Hq, splits]
   int* counters;    // [T * Hkv] split arrival counters, kept at zero between launches
+  unsigned long long* trace;  // optional per-CTA phase timestamps (profiling)
 };
 
 constexpr float LOG2E = 1.4426950408889634f;
@@ -219,14 +221,80 @@ BRAID_DEVICE void softmax_update(float (*s)[4], float* m, float* l, float (*acc)
 }
 
 // --------------------------------------------------------------- decode
-template <int D>
-__global__ void __launch_bounds__(128) attn_decode_kernel(const AttnParams p) {
-  extern __shared__ __align__(128) uint8_t sm[];
-  uint8_t* qs = sm;                                  // [16][D]
-  uint8_t* kbuf = sm + 16 * D * 2;                   // 2 x [64][D]
-  uint8_t* vbuf = kbuf + 2 * KT * D * 2;             // 2 x [64][D]
+// Byte offset of 16-byte chunk c (of D/8) in row r of a TMA-written tile
+// stored as D/64 column halves of [ROWS x 128 B] with 128-byte swizzle.
+template <int ROWS>
+BRAID_DEVICE uint32_t tswz(int r, int c) {
+  return (uint32_t)((c >> 3) * (ROWS * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
+
+// Producer cursor over the (segment, 64-key tile) sequence of one split range,
+// walked by warp 0; page ids are fetched 32 at a time into registers and
+// broadcast with shuffles (no dependent global load per box).
+struct ProdCursor {
+  int s, s1, segstart, lo, hi, off, sl, npages, win, win_page;
+  const int* pages;
+};
+
+BRAID_DEVICE bool pc_settle(const AttnParams& p, ProdCursor& c, int r0, int r1) {
+  while (c.s < c.s1 && c.segstart < r1) {
+    const int len = p.seg_len[c.s];
+    c.lo = max(r0 - c.segstart, 0);
+    c.hi = min(r1 - c.segstart, len);
+    if (c.lo < c.hi) {
+      c.off = p.seg_offset[c.s];
+      c.pages = p.page_ids + p.seg_page_indptr[c.s];
+      c.npages = p.seg_page_indptr[c.s + 1] - p.seg_page_indptr[c.s];
+      c.sl = (c.off + c.lo) & ~(KT - 1);
+      c.win = -(1 << 30);
+      return true;
+    }
+    c.segstart += len;
+    ++c.s;
+  }
+  c.s = c.s1;
+  return false;
+}
+
+BRAID_DEVICE void pc_next(const AttnParams& p, ProdCursor& c, int r0, int r1) {
+  c.sl += KT;
+  if (c.sl < c.off + c.hi) return;
+  c.segstart += p.seg_len[c.s];
+  ++c.s;
+  pc_settle(p, c, r0, r1);
+}
+
+// Decode attention.  Four warps; warp 0 also streams 64-key K/V tiles with TMA
+// into a STAGES-deep mbarrier ring (boxes of BR rows x 64 columns; BR = 64 when
+// the page size is a multiple of 64, else 16 so a box never straddles a page),
+// issuing tile i+STAGES-1 just before the CTA computes tile i.  Each warp takes
+// 16 keys of every tile (mma.sync, fp32 online softmax).  Tiles are aligned in
+// slot space; keys outside the segment or the split range are masked.
+template <int D, int STAGES, int BR>
+__global__ void __launch_bounds__(128, 2) attn_decode_kernel(const __grid_constant__ CUtensorMap tmkv,
+                                                             const AttnParams p) {
+  constexpr int TILE = KT * D * 2;  // bytes of one K (or V) tile
+  extern __shared__ uint8_t sm_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* kbuf = sm;                         // STAGES x TILE
+  uint8_t* vbuf = sm + STAGES * TILE;         // STAGES x TILE
+  uint8_t* qs = vbuf + STAGES * TILE;         // [16][D] bf16, tswz<16> layout
+  uint64_t* full = reinterpret_cast<uint64_t*>(qs + 16 * D * 2);
+  uint64_t* empty = full + STAGES;
   const int b = blockIdx.x, kh = blockIdx.y, split = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  unsigned long long* tr = p.trace
+      ? p.trace + 8 * ((size_t)(blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) : nullptr;
+  if (threadIdx.x == 0) {
+    if (tr != nullptr) tr[0] = globaltimer_ns();
+    tma_prefetch_desc(&tmkv);
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 4);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
   pdl_wait();
   pdl_trigger();
   const int t = p.qo_indptr[b];
@@ -238,52 +306,155 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnParams p) {
   int per = (total + p.num_splits - 1) / p.num_splits;
   per = (per + KT - 1) / KT * KT;
   const int r0 = split * per, r1 = min(total, r0 + per);
+  const int G = p.G;
+
+  // warp 0: issue one tile into stage st (all lanes take part in the page lookup)
+  ProdCursor pc{s0, s1, 0, 0, 0, 0, 0, 0, 0, 0, nullptr};
+  auto issue = [&](int st) {
+#pragma unroll
+    for (int q = 0; q < KT / BR; ++q) {
+      const int slot = pc.sl + q * BR;
+      const int pidx = min(slot / p.PS, pc.npages - 1);
+      if (pidx < pc.win || pidx >= pc.win + 32) {
+        pc.win = pidx;
+        pc.win_page = pc.win + lane < pc.npages ? pc.pages[pc.win + lane] : 0;
+      }
+      const int page = __shfl_sync(0xffffffffu, pc.win_page, pidx - pc.win);
+      if (lane == 0) {
+        const int row_k = ((page * 2 + 0) * p.Hkv + kh) * p.PS + slot % p.PS;
+        const int row_v = row_k + p.Hkv * p.PS;
+#pragma unroll
+        for (int h = 0; h < D / 64; ++h) {
+          tma_load_2d(kbuf + st * TILE + h * (KT * 128) + q * BR * 128, &tmkv, &full[st], h * 64, row_k);
+          tma_load_2d(vbuf + st * TILE + h * (KT * 128) + q * BR * 128, &tmkv, &full[st], h * 64, row_v);
+        }
+      }
+    }
+  };
+  int issued = 0;
+  if (warp == 0) {
+    bool v = pc_settle(p, pc, r0, r1);
+    for (; issued < STAGES - 1 && v; ++issued) {
+      if (lane == 0) mbar_arrive_expect_tx(&full[issued], 2 * TILE);
+      issue(issued);
+      pc_next(p, pc, r0, r1);
+      v = pc.s < pc.s1;
+    }
+  }
 
   float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
   float acc[D / 8][4];
 #pragma unroll
   for (int i = 0; i < D / 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
   uint32_t qf[D / 16][4];
-  const int G = p.G;
-
-  int segstart = 0;
-  for (int s = s0; s < s1 && segstart < r1; ++s) {
+  int it = 0, segstart = 0;
+  bool ok = true;
+  for (int s = s0; s < s1 && segstart < r1 && ok; ++s) {
     const int len = p.seg_len[s];
     const int lo = max(r0 - segstart, 0), hi = min(r1 - segstart, len);
     if (lo < hi) {
       __syncthreads();
-      build_q_tile<D>(p, kh, p.seg_delta[s], G, 16, qs, [&](int r, int& tok, int& g) { tok = t; g = r; });
-      load_kv_tile<D>(p, s, kh, lo, hi, kbuf, vbuf);
-      cp_async_commit();
-      __syncthreads();
-      load_q_frags<D>(qs, 0, qf);
-      const int pos0 = p.seg_pos0[s];
-      int buf = 0;
-      for (int j0 = lo; j0 < hi; j0 += KT) {
-        if (j0 + KT < hi) {
-          load_kv_tile<D>(p, s, kh, j0 + KT, hi, kbuf + (buf ^ 1) * KT * D * 2, vbuf + (buf ^ 1) * KT * D * 2);
-          cp_async_commit();
-          cp_async_wait<1>();
-        } else {
-          cp_async_wait<0>();
+      {
+        // query rows rotated for this segment: one position for every row,
+        // all loads independent (issued together)
+        constexpr int H2 = D / 2;
+        int pos = qpos - p.seg_delta[s];
+        pos = pos < 0 ? 0 : (pos >= p.rope_len ? p.rope_len - 1 : pos);
+        __nv_bfloat16* qt = reinterpret_cast<__nv_bfloat16*>(qs);
+#pragma unroll
+        for (int k = 0; k < 16 * H2 / 128; ++k) {
+          const int i = threadIdx.x + 128 * k;
+          const int r = i / H2, d = i % H2;
+          float x1 = 0.f, x2 = 0.f;
+          if (r < G) {
+            const __nv_bfloat16* qp = p.q + ((size_t)t * p.Hq + kh * G + r) * D;
+            const float a = bf2f(qp[d]), bb = bf2f(qp[d + H2]);
+            if (p.use_rope) {
+              const float cs = p.cos[(size_t)pos * H2 + d], sn = p.sin[(size_t)pos * H2 + d];
+              x1 = a * cs - bb * sn;
+              x2 = bb * cs + a * sn;
+            } else {
+              x1 = a;
+              x2 = bb;
+            }
+          }
+          qt[(tswz<16>(r, d / 8) >> 1) + (d & 7)] = f2bf(x1);
+          qt[(tswz<16>(r, (d + H2) / 8) >> 1) + ((d + H2) & 7)] = f2bf(x2);
         }
-        __syncthreads();
-        const uint8_t* ks = kbuf + buf * KT * D * 2;
-        const uint8_t* vs = vbuf + buf * KT * D * 2;
+      }
+      __syncthreads();
+      {
+        const int r = (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          ldsm_x4(smem_u32(qs) + tswz<16>(r, kk * 2 + (lane >> 4)), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+      }
+      if (tr != nullptr && threadIdx.x == 0 && tr[1] == 0) tr[1] = globaltimer_ns();
+      const int off = p.seg_offset[s], pos0 = p.seg_pos0[s];
+      for (int sl = (off + lo) & ~(KT - 1); sl < off + hi; sl += KT, ++it) {
+        // refill: tile `issued` goes into the stage released after tile it-1
+        if (warp == 0 && pc.s < pc.s1) {
+          const int st2 = issued % STAGES;
+          int okw = 1;
+          if (lane == 0) {
+            if (issued >= STAGES) okw = mbar_wait(&empty[st2], ((issued / STAGES) & 1) ^ 1) ? 1 : 0;
+            if (okw) mbar_arrive_expect_tx(&full[st2], 2 * TILE);
+          }
+          if (__shfl_sync(0xffffffffu, okw, 0)) {
+            issue(st2);
+            pc_next(p, pc, r0, r1);
+            ++issued;
+          } else {
+            pc.s = pc.s1;
+          }
+        }
+        const int st = it % STAGES;
+        if (!mbar_wait(&full[st], (it / STAGES) & 1)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* ks = kbuf + st * TILE;
+        const uint8_t* vs = vbuf + st * TILE;
         float sc[2][4];
-        qk_tile<D, 2>(qf, ks, warp * 16, sc);
+#pragma unroll
+        for (int nb = 0; nb < 2; ++nb) {
+          sc[nb][0] = sc[nb][1] = sc[nb][2] = sc[nb][3] = 0.f;
+          const int row = warp * 16 + nb * 8 + (lane & 7);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; kk += 2) {
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4(smem_u32(ks) + tswz<KT>(row, kk * 2 + (lane >> 3)), b0, b1, b2, b3);
+            mma16816(sc[nb], qf[kk], b0, b1);
+            mma16816(sc[nb], qf[kk + 1], b2, b3);
+          }
+        }
 #pragma unroll
         for (int nb = 0; nb < 2; ++nb)
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const int j = j0 + warp * 16 + nb * 8 + 2 * (lane & 3) + (e & 1);
-            const bool vis = j < hi && pos0 + j <= qpos;
+            const int j = sl + warp * 16 + nb * 8 + 2 * (lane & 3) + (e & 1) - off;  // segment-local key
+            const bool vis = j >= lo && j < hi && pos0 + j <= qpos;
             sc[nb][e] = vis ? sc[nb][e] * p.scale_log2 : -INFINITY;
           }
         softmax_update<2, D>(sc, m, l, acc);
-        pv_tile<D, 1>(sc, vs, warp * 16, acc);
-        __syncthreads();
-        buf ^= 1;
+        {
+          uint32_t a[4];
+          a[0] = pack_bf16(sc[0][0], sc[0][1]);
+          a[1] = pack_bf16(sc[0][2], sc[0][3]);
+          a[2] = pack_bf16(sc[1][0], sc[1][1]);
+          a[3] = pack_bf16(sc[1][2], sc[1][3]);
+          const int row = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+          for (int nb = 0; nb < D / 8; nb += 2) {
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4_t(smem_u32(vs) + tswz<KT>(row, nb + (lane >> 4)), b0, b1, b2, b3);
+            mma16816(acc[nb], a, b0, b1);
+            mma16816(acc[nb + 1], a, b2, b3);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+        if (tr != nullptr && threadIdx.x == 0 && tr[2] == 0) tr[2] = globaltimer_ns();
       }
     }
     segstart += len;
@@ -291,6 +462,8 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnParams p) {
 
   // ---- merge the 4 warps' partial states (reuse the K/V buffers)
   __syncthreads();
+  if (tr != nullptr && threadIdx.x == 0) tr[3] = globaltimer_ns();
+  constexpr int AW_LD = D + 4;  // padded rows: no bank conflicts
   float* mw = reinterpret_cast<float*>(kbuf);        // [4][16]
   float* lw = mw + 64;                                // [4][16]
   float* aw = lw + 64;                                // [4][16][D]
@@ -304,13 +477,13 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnParams p) {
 #pragma unroll
   for (int nb = 0; nb < D / 8; ++nb) {
     const int d = nb * 8 + 2 * c;
-    aw[(warp * 16 + g) * D + d] = acc[nb][0];
-    aw[(warp * 16 + g) * D + d + 1] = acc[nb][1];
-    aw[(warp * 16 + g + 8) * D + d] = acc[nb][2];
-    aw[(warp * 16 + g + 8) * D + d + 1] = acc[nb][3];
+    aw[(warp * 16 + g) * AW_LD + d] = acc[nb][0];
+    aw[(warp * 16 + g) * AW_LD + d + 1] = acc[nb][1];
+    aw[(warp * 16 + g + 8) * AW_LD + d] = acc[nb][2];
+    aw[(warp * 16 + g + 8) * AW_LD + d + 1] = acc[nb][3];
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+  for (int i = threadIdx.x; i < G * D; i += 128) {
     const int row = i / D, d = i % D;
     float M = -INFINITY;
     for (int w = 0; w < 4; ++w) M = fmaxf(M, mw[w * 16 + row]);
@@ -319,7 +492,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnParams p) {
       for (int w = 0; w < 4; ++w) {
         const float e = exp2f(mw[w * 16 + row] - M);
         L += lw[w * 16 + row] * e;
-        O += aw[(w * 16 + row) * D + d] * e;
+        O += aw[(w * 16 + row) * AW_LD + d] * e;
       }
     }
     const int h = kh * G + row;
@@ -331,6 +504,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnParams p) {
       if (d == 0) p.part_lse[idx] = L > 0.f ? M + log2f(L) : -INFINITY;
     }
   }
+  if (tr != nullptr && threadIdx.x == 0) tr[4] = globaltimer_ns();
   if (p.num_splits == 1) return;
   // ---- the last split CTA of (token, kv head) merges every split's partial
   __shared__ int s_last;
@@ -346,21 +520,33 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnParams p) {
   if (!s_last) return;
   __threadfence();
   const int ns = p.num_splits;
-  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+  for (int i = threadIdx.x; i < G * D; i += 128) {
     const int row = i / D, d = i % D;
     const size_t base = ((size_t)t * p.Hq + kh * G + row) * ns;
+    float lse[32], o[32];
+#pragma unroll
+    for (int q = 0; q < 32; ++q)
+      if (q < ns) {
+        lse[q] = __ldcg(p.part_lse + base + q);
+        o[q] = __ldcg(p.part_o + (base + q) * D + d);
+      }
     float M = -INFINITY;
-    for (int s = 0; s < ns; ++s) M = fmaxf(M, __ldcg(p.part_lse + base + s));
+#pragma unroll
+    for (int q = 0; q < 32; ++q)
+      if (q < ns) M = fmaxf(M, lse[q]);
     float W = 0.f, O = 0.f;
     if (M != -INFINITY) {
-      for (int s = 0; s < ns; ++s) {
-        const float w = exp2f(__ldcg(p.part_lse + base + s) - M);
-        W += w;
-        O += w * __ldcg(p.part_o + (base + s) * D + d);
-      }
+#pragma unroll
+      for (int q = 0; q < 32; ++q)
+        if (q < ns) {
+          const float w = exp2f(lse[q] - M);
+          W += w;
+          O += w * o[q];
+        }
     }
     p.out[(size_t)t * p.Hq * D + (kh * G + row) * D + d] = f2bf(W > 0.f ? O / W : 0.f);
   }
+  if (tr != nullptr && threadIdx.x == 0) tr[5] = globaltimer_ns();
 }
 
 // -------------------------------------------------------------- prefill
@@ -467,6 +653,12 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const AttnParams p) {
 }
 
 // ------------------------------------------------------------------ host
+static unsigned long long* g_attn_trace = nullptr;
+// Profiling: per-CTA phase timestamps of subsequent decode launches (int64 [8 * CTAs]).
+void attn_set_trace(torch::Tensor buf) {
+  g_attn_trace = buf.defined() && buf.numel() ? reinterpret_cast<unsigned long long*>(buf.data_ptr<int64_t>()) : nullptr;
+}
+
 // Per-device split-merge counters (zeroed once; the merging CTA re-arms its counter).
 static int* attn_counters(int dev, size_t n) {
   static std::mutex mu;
@@ -485,16 +677,32 @@ static int* attn_counters(int dev, size_t n) {
 }
 
 template <int D>
-static void launch_attn(AttnParams& p, int num_seqs, int max_q_len, bool decode, int T, cudaStream_t st) {
+static void launch_attn(AttnParams& p, int num_seqs, int max_q_len, bool decode, int T, int64_t P,
+                        cudaStream_t st) {
   if (decode) {
-    const int smem = 16 * D * 2 + 4 * KT * D * 2;
-    auto k = attn_decode_kernel<D>;
-    static bool attr = false;
-    if (!attr) {
-      C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      attr = true;
+    constexpr int STAGES = D == 128 ? 3 : 4;
+    const int smem = 2 * STAGES * KT * D * 2 + 16 * D * 2 + 2 * STAGES * 8 + 1024;
+    // the layer pool viewed as rows of D elements: row = ((page*2 + kv)*Hkv + kh)*PS + slot
+    const int64_t rows = P * 2 * p.Hkv * p.PS;
+    if (p.PS % 64 == 0) {
+      auto k = attn_decode_kernel<D, STAGES, 64>;
+      static bool attr = false;
+      if (!attr) {
+        C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        attr = true;
+      }
+      CUtensorMap tm = make_tmap(p.kv, rows, D, D, 64);
+      launch_pdl(k, dim3(num_seqs, p.Hkv, p.num_splits), dim3(128), smem, st, tm, p);
+    } else {
+      auto k = attn_decode_kernel<D, STAGES, 16>;
+      static bool attr = false;
+      if (!attr) {
+        C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        attr = true;
+      }
+      CUtensorMap tm = make_tmap(p.kv, rows, D, D, 16);
+      launch_pdl(k, dim3(num_seqs, p.Hkv, p.num_splits), dim3(128), smem, st, tm, p);
     }
-    launch_pdl(k, dim3(num_seqs, p.Hkv, p.num_splits), dim3(128), smem, st, p);
   } else {
     const int smem = 64 * D * 2 + 4 * KT * D * 2;
     auto k = attn_prefill_kernel<D>;
@@ -521,6 +729,7 @@ void attention(torch::Tensor out, torch::Tensor q, torch::Tensor kv, torch::Tens
   TORCH_CHECK(kv.size(4) == D && Hq % Hkv == 0, "attention: head layout mismatch");
   const int G = Hq / Hkv;
   TORCH_CHECK(G <= 16 || !decode, "attention: decode supports up to 16 query heads per KV head");
+  TORCH_CHECK(PS % 16 == 0, "attention: page size must be a multiple of 16");
   if (T == 0 || num_seqs == 0) return;
   const at::cuda::CUDAGuard guard(q.device());
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
@@ -547,6 +756,7 @@ void attention(torch::Tensor out, torch::Tensor q, torch::Tensor kv, torch::Tens
   p.G = G;
   p.PS = PS;
   p.num_splits = decode ? (int)std::max<int64_t>(1, num_splits) : 1;
+  p.trace = decode ? g_attn_trace : nullptr;
   torch::Tensor po, pl;
   if (p.num_splits > 1) {
     if (part_o.has_value() && part_o->defined() && part_o->numel() >= (int64_t)T * Hq * p.num_splits * D) {
@@ -561,9 +771,9 @@ void attention(torch::Tensor out, torch::Tensor q, torch::Tensor kv, torch::Tens
     p.counters = attn_counters(q.get_device(), (size_t)T * Hkv);
   }
   if (D == 128)
-    launch_attn<128>(p, num_seqs, max_q_len, decode, T, st);
+    launch_attn<128>(p, num_seqs, max_q_len, decode, T, kv.size(0), st);
   else if (D == 64)
-    launch_attn<64>(p, num_seqs, max_q_len, decode, T, st);
+    launch_attn<64>(p, num_seqs, max_q_len, decode, T, kv.size(0), st);
   else
     TORCH_CHECK(false, "attention: head_dim must be 64 or 128");
 }

@@ -9,6 +9,7 @@ void gemm_qkv(torch::Tensor q_out, torch::Tensor x, torch::Tensor w, c10::option
               c10::optional<torch::Tensor> q_norm, c10::optional<torch::Tensor> k_norm, double head_eps,
               torch::Tensor cos, torch::Tensor sin, int64_t Hq, int64_t Hkv, int64_t D, bool use_rope);
 int64_t gemm_check_error(int64_t device);
+void gemm_set_trace(torch::Tensor buf);
 int64_t gemm_push(torch::Tensor x, torch::Tensor w, torch::Tensor peers, int64_t flags_off, int64_t rank, int64_t tp,
                   int64_t maxT, torch::Tensor epoch_state);
 std::vector<torch::Tensor> comm_alloc(int64_t nbytes, int64_t device);
@@ -26,6 +27,7 @@ void attention(torch::Tensor out, torch::Tensor q, torch::Tensor kv, torch::Tens
                torch::Tensor page_ids, torch::Tensor cos, torch::Tensor sin, double scale, bool use_rope,
                int64_t num_seqs, int64_t max_q_len, int64_t max_kv_len, bool decode, int64_t num_splits,
                c10::optional<torch::Tensor> part_o, c10::optional<torch::Tensor> part_lse);
+void attn_set_trace(torch::Tensor buf);
 void rms_norm(torch::Tensor out, torch::Tensor x, torch::Tensor w, double eps);
 void add_rms_norm(torch::Tensor out, torch::Tensor residual, torch::Tensor x, torch::Tensor w, double eps);
 void layer_norm(torch::Tensor out, torch::Tensor x, torch::Tensor w, torch::Tensor b, double eps);
@@ -50,8 +52,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("comm_free", &braid::comm_free);
   m.def("tp_push", &braid::tp_push, "push a bf16 partial to every TP peer");
   m.def("tp_reduce_add", &braid::tp_reduce_add, "bounded-wait sum of pushed partials (+ residual)");
+  m.def("gemm_set_trace", &braid::gemm_set_trace, "profiling: per-CTA phase timestamps of later GEMMs");
   m.def("gemm_check_error", &braid::gemm_check_error, "read and clear the GEMM bounded-wait error flag");
   m.def("attention", &braid::attention, "paged cascade attention (decode/prefill)");
+  m.def("attn_set_trace", &braid::attn_set_trace, "profiling: per-CTA phase timestamps of later decode attention");
   m.def("rms_norm", &braid::rms_norm);
   m.def("add_rms_norm", &braid::add_rms_norm);
   m.def("layer_norm", &braid::layer_norm);

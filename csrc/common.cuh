@@ -79,6 +79,34 @@ BRAID_DEVICE bool mbar_wait(uint64_t* bar, uint32_t phase, uint64_t timeout_ns =
 BRAID_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 BRAID_DEVICE void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// Thread-block cluster helpers (distributed shared memory).
+BRAID_DEVICE void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+BRAID_DEVICE uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory offset in CTA `rank` of this cluster.
+BRAID_DEVICE uint32_t dsmem_map(uint32_t smem_addr, uint32_t rank) {
+  uint32_t d;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(smem_addr), "r"(rank));
+  return d;
+}
+// Volatile (kept in program order relative to the cluster barriers) but
+// without a memory clobber, so consecutive loads are issued back to back.
+BRAID_DEVICE float4 dsmem_ld_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+  return v;
+}
+
+// GPU-scope acquire/release fence.  After a CTA barrier, one thread's fence is
+// cumulative over the writes the barrier ordered before it (release side);
+// before a CTA barrier it orders the other threads' later reads (acquire side).
+BRAID_DEVICE void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
 BRAID_DEVICE void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }

@@ -81,11 +81,13 @@ struct GemmArgs {
   float rs_eps;
   int splits;
   int kb_per_split;
-  float* ws;          // split-K partials
+  int cluster;        // 1: the split-K CTAs of a tile form one cluster and reduce through DSMEM
+  float* ws;          // split-K partials (global path)
   int* counters;      // one per output tile, kept at zero between launches
   int* err;           // error flag (bounded-wait timeout)
   QkvEpi qkv;
   PushEpi push;
+  unsigned long long* trace;  // optional per-CTA phase timestamps (profiling)
 };
 
 constexpr int BM = 128;
@@ -146,6 +148,8 @@ BRAID_DEVICE void qkv_head_store(const QkvEpi& q, float* v, int head, int t, int
   for (int i = 0; i < E; ++i) dst[i] = f2bf(v[i]);
 }
 
+BRAID_DEVICE bool et_is_epi_last(int tid) { return tid == 191; }
+
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
                                                                const __grid_constant__ CUtensorMap tmB,
@@ -171,6 +175,9 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
   const int kb0 = split * args.kb_per_split;
   const int nkb = min(args.kb_per_split, kb_total - kb0);
   constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
+  unsigned long long* tr = args.trace
+      ? args.trace + 8 * ((size_t)(blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) : nullptr;
+  if (tr != nullptr && threadIdx.x == 0) tr[0] = globaltimer_ns();
 
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
@@ -191,6 +198,15 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
   pdl_trigger();
+  // epilogue-thread geometry (used by warps 2..5 only)
+  const int wq = warp & 3;             // TMEM lane quarter this warp may access
+  const int r = wq * 32 + lane;        // row of the tile owned by this thread
+  const int et = threadIdx.x - 64;     // 0..127 epilogue thread id
+  const int ew = et >> 5;              // epilogue warp 0..3
+  const uint32_t trow = tmem + ((uint32_t)(wq * 32) << 16);
+  const int tile = m_tile * gridDim.y + n_tile;
+  float rs_row = 1.f;
+  bool has_acc = false;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -218,12 +234,14 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+      if (tr != nullptr) tr[1] = globaltimer_ns();
       for (int i = 0; i < nkb; ++i) {
         const int s = i % STAGES;
         if (!mbar_wait(&full[s], (i / STAGES) & 1)) {
           atomicExch(args.err, 2);
           break;
         }
+        if (tr != nullptr && i == 0) tr[2] = globaltimer_ns();
         tc_fence_after();
         const uint64_t ad = smem_desc_sw128(smem_u32(ringA + s * S::A_BYTES));
         const uint64_t bd = smem_desc_sw128(smem_u32(ringB + s * S::B_BYTES));
@@ -236,13 +254,8 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int wq = warp & 3;             // TMEM lane quarter this warp may access
-    const int r = wq * 32 + lane;        // row of the tile owned by this thread
-    const int et = threadIdx.x - 64;     // 0..127 epilogue thread id
-    const int ew = et >> 5;              // epilogue warp 0..3
     pdl_wait();
     // Fused input RMSNorm: 1/rms of every token of the tile (overlaps the mainloop).
-    float rs_row = 1.f;
     if (args.rs_x != nullptr) {
       if (args.swap) {
         for (int tt = ew; tt < BN; tt += 4) {
@@ -278,14 +291,33 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
     }
     const bool ready = mbar_wait(tmem_full, 0);
     if (!ready) atomicExch(args.err, 3);
+    if (tr != nullptr && et == 0) tr[3] = globaltimer_ns();
     tc_fence_after();
-    const uint32_t trow = tmem + ((uint32_t)(wq * 32) << 16);
-    const int tile = m_tile * gridDim.y + n_tile;
-    const bool has_acc = ready && nkb > 0;
-
-    // Split-K: publish this slice's partial, elect the last CTA of the tile.
-    bool last = true;
-    if (args.splits > 1) {
+    has_acc = ready && nkb > 0;
+    if (args.cluster) {
+      // Cluster split-K: stage this slice's fp32 partial in the (now idle) A ring.
+      float* part = reinterpret_cast<float*>(ringA) + (size_t)r * BN;
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        float v[16];
+        if (has_acc) {
+          tmem_ld16(trow + c0, v);
+          tc_wait_ld();
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 16; j += 4)
+          *reinterpret_cast<float4*>(part + c0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+      }
+    }
+  }
+  // Every thread of every CTA of the cluster: the partials are now visible.
+  if (args.cluster) cluster_sync_all();
+  if (warp >= 2) {
+    // Split-K (global path): publish this slice's partial, elect the last CTA of the tile.
+    bool last = args.cluster ? cluster_rank() == 0 : true;
+    if (args.splits > 1 && !args.cluster) {
       float* mine = args.ws + ((size_t)(tile * args.splits + split) * BM + r) * BN;
       for (int c0 = 0; c0 < BN; c0 += 16) {
         float v[16];
@@ -300,32 +332,62 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
         for (int j = 0; j < 16; j += 4)
           *reinterpret_cast<float4*>(mine + c0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
       }
-      __threadfence();
       named_bar_sync(1, 128);
       if (et == 0) {
+        fence_acq_rel_gpu();  // release this CTA's partial (cumulative over the barrier)
         const int old = atomicAdd(&args.counters[tile], 1);
         *s_flag = (old == args.splits - 1);
-        if (old == args.splits - 1) args.counters[tile] = 0;
+        if (old == args.splits - 1) {
+          args.counters[tile] = 0;
+          fence_acq_rel_gpu();  // acquire the other slices' partials
+        }
       }
       named_bar_sync(1, 128);
       last = *s_flag != 0;
-      __threadfence();
     }
 
     if (last) {
       // Columns [c0, c0+16) of this thread's row: split-K sum, times 1/rms of
       // the token, plus bias (bias before any rounding, as in an HF linear).
       auto load_cols = [&](int c0, float* v) {
-        if (args.splits > 1) {
+        if (args.cluster) {
+          // all splits' partials of 4 columns are requested before any is summed
+          const uint32_t mine = smem_u32(reinterpret_cast<float*>(ringA) + (size_t)r * BN + c0);
+          const int ns = args.splits;
+#pragma unroll
+          for (int j = 0; j < 16; j += 4) {
+            float4 f[16];
+#pragma unroll
+            for (int q = 0; q < 16; ++q)
+              if (q < ns) f[q] = dsmem_ld_f4(dsmem_map(mine, (uint32_t)q) + 4 * j);
+            float4 acc4 = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int q = 0; q < 16; ++q)
+              if (q < ns) {
+                acc4.x += f[q].x; acc4.y += f[q].y; acc4.z += f[q].z; acc4.w += f[q].w;
+              }
+            v[j] = acc4.x; v[j + 1] = acc4.y; v[j + 2] = acc4.z; v[j + 3] = acc4.w;
+          }
+        } else if (args.splits > 1) {
 #pragma unroll
           for (int j = 0; j < 16; ++j) v[j] = 0.f;
-          for (int s = 0; s < args.splits; ++s) {
-            const float* p = args.ws + ((size_t)(tile * args.splits + s) * BM + r) * BN + c0;
+          for (int s0 = 0; s0 < args.splits; s0 += 8) {
+            float4 f[8][4];
 #pragma unroll
-            for (int j = 0; j < 16; j += 4) {
-              const float4 q = __ldcg(reinterpret_cast<const float4*>(p + j));
-              v[j] += q.x; v[j + 1] += q.y; v[j + 2] += q.z; v[j + 3] += q.w;
-            }
+            for (int q = 0; q < 8; ++q)
+              if (s0 + q < args.splits) {
+                const float* p = args.ws + ((size_t)(tile * args.splits + s0 + q) * BM + r) * BN + c0;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) f[q][j] = __ldcg(reinterpret_cast<const float4*>(p + 4 * j));
+              }
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              if (s0 + q < args.splits) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  v[4 * j] += f[q][j].x; v[4 * j + 1] += f[q][j].y; v[4 * j + 2] += f[q][j].z; v[4 * j + 3] += f[q][j].w;
+                }
+              }
           }
         } else if (has_acc) {
           tmem_ld16(trow + c0, v);
@@ -552,6 +614,9 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
     }
   }
 
+  // keep this CTA's partial alive until the cluster leader has read it
+  if (args.cluster) cluster_sync_all();
+  if (tr != nullptr && et_is_epi_last(threadIdx.x)) tr[4] = globaltimer_ns();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -580,7 +645,7 @@ static EncodeTiledFn get_encode() {
 
 // Row-major bf16 matrix [rows, cols] with leading dimension ld (elements);
 // box = [64 cols (128 bytes), box_rows], 128-byte swizzle, zero OOB fill.
-static CUtensorMap make_tmap(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+CUtensorMap make_tmap(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
   struct Key {
     const void* p; int64_t r, c, ld; int br;
     bool operator==(const Key& o) const { return p == o.p && r == o.r && c == o.c && ld == o.ld && br == o.br; }
@@ -658,9 +723,11 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs&
   static bool attr = false;
   if (!attr) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
     attr = true;
   }
-  launch_pdl(kern, grid, dim3(192), S::TOTAL, st, ta, tb, a);
+  launch_pdl_cluster(kern, grid, dim3(192), S::TOTAL, st, a.cluster ? dim3(1, 1, a.splits) : dim3(1, 1, 1), ta, tb,
+                     a);
 }
 
 static int num_sms() {
@@ -671,6 +738,13 @@ static int num_sms() {
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
   }
   return n;
+}
+
+static unsigned long long* g_trace = nullptr;
+// Profiling: record per-CTA phase timestamps of subsequent GEMM launches into
+// `buf` (int64 [8 * CTAs]); an empty tensor switches recording off.
+void gemm_set_trace(torch::Tensor buf) {
+  g_trace = buf.defined() && buf.numel() ? reinterpret_cast<unsigned long long*>(buf.data_ptr<int64_t>()) : nullptr;
 }
 
 static inline const __nv_bfloat16* opt_bf(const c10::optional<torch::Tensor>& t) {
@@ -716,16 +790,30 @@ static void run_gemm(GemmArgs& a, const torch::Tensor& x, const torch::Tensor& w
   // covers the machine; decode shapes have few output tiles.
   int splits = 1;
   const int slots = num_sms() * (swap ? 2 : 1);
-  if (tiles < slots) splits = std::max(1, std::min({slots / tiles, kb_total / 2, 32}));
+  if (tiles < slots) splits = std::max(1, std::min({slots / tiles, kb_total / 2, 16}));
+  static const int forced = [] {  // tuning knob: BRAID_GEMM_SPLITS=n forces the split-K factor
+    const char* e = getenv("BRAID_GEMM_SPLITS");
+    return e ? atoi(e) : 0;
+  }();
+  if (forced > 0) splits = std::max(1, std::min(forced, kb_total));
   int kbps = (kb_total + splits - 1) / splits;
   splits = (kb_total + kbps - 1) / kbps;
   a.splits = splits;
   a.kb_per_split = kbps;
+  // Optional (BRAID_GEMM_CLUSTER=1): up to 16 K-slices reduce through
+  // distributed shared memory inside one thread-block cluster.  Measured
+  // slower than the global workspace on B200 for decode shapes, so off by default.
+  static const bool use_cluster = [] {
+    const char* e = getenv("BRAID_GEMM_CLUSTER");
+    return e && e[0] == '1';
+  }();
+  a.cluster = (splits > 1 && splits <= 16 && use_cluster) ? 1 : 0;
   const int dev = x.get_device();
   SplitKScratch& sc = scratch_for(dev, splits > 1 ? (size_t)tiles * splits * BM * BN * 4 : 0, tiles);
   a.ws = sc.ws;
   a.counters = sc.counters;
   a.err = sc.err;
+  a.trace = g_trace;
   dim3 grid(m_tiles, n_tiles, splits);
   const void* pa = swap ? w.data_ptr() : x.data_ptr();
   const void* pb = swap ? x.data_ptr() : w.data_ptr();
