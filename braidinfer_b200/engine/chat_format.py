@@ -27,6 +27,7 @@ class ChatFormat:
     def __init__(self, tokenizer, use_template: bool = True):
         self.tok = tokenizer
         self.enabled = bool(use_template and tokenizer is not None and getattr(tokenizer, "chat_template", None))
+        self._gen_prompt: Optional[List[int]] = None
 
     def _render(self, msgs, gen: bool = False) -> str:
         return self.tok.apply_chat_template(msgs, tokenize=False, add_generation_prompt=gen)
@@ -50,8 +51,12 @@ class ChatFormat:
         return self.encode(self.fragment(role or ROLE_OF[chunk_type], content))
 
     def generation_prompt(self) -> List[int]:
-        if not self.enabled:
-            return []
-        msgs = [_DUMMY_SYS, {"role": "user", "content": "x"}]
-        a, b = self._render(msgs, False), self._render(msgs, True)
-        return self.encode(b[len(a):]) if b.startswith(a) else []
+        """Tokens that open the assistant turn (rendered once, then cached)."""
+        if self._gen_prompt is None:
+            if not self.enabled:
+                self._gen_prompt = []
+            else:
+                msgs = [_DUMMY_SYS, {"role": "user", "content": "x"}]
+                a, b = self._render(msgs, False), self._render(msgs, True)
+                self._gen_prompt = self.encode(b[len(a):]) if b.startswith(a) else []
+        return list(self._gen_prompt)

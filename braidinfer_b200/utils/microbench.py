@@ -1,0 +1,176 @@
+"""Kernel micro-benchmarks and profiler entry points (device time, CUDA events).
+
+    python -m braidinfer_b200.utils.microbench gemm M N K [--epi 0|1] [--graph]
+    python -m braidinfer_b200.utils.microbench attn-decode B L HQ HKV [--splits S]
+    python -m braidinfer_b200.utils.microbench attn-prefill L HQ HKV [--batch B]
+    python -m braidinfer_b200.utils.microbench decode-step MODEL B PROMPT_LEN
+
+``decode-step`` runs one eager decode step of a random-init model between
+``cudaProfilerStart``/``Stop`` (for ``ncu --profile-from-start off``).  Timings
+are taken after warm-up with CUDA events on the launching stream; ``--graph``
+replays 20 back-to-back launches from a CUDA graph (the decode setting).
+"""
+from __future__ import annotations
+
+import argparse
+import math
+
+import torch
+
+
+def _graph_time(fn, n: int = 20) -> float:
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(n):
+            fn()
+    g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / n * 1e3
+
+
+def _eager_time(fn, n: int = 10) -> float:
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(n):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / n * 1e3
+
+
+def bench_gemm(M: int, N: int, K: int, epi: int = 0, graph: bool = False) -> dict:
+    from ..ops._ext import ext
+
+    x = torch.randn(M, K, device="cuda").bfloat16()
+    w = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
+    out = torch.empty(M, N // 2 if epi else N, device="cuda", dtype=torch.bfloat16)
+    fn = lambda: ext().gemm(out, x, w, None, None, epi, -1.0)  # noqa: E731
+    us = (_graph_time if graph else _eager_time)(fn)
+    return {"kernel": "gemm_tcgen05", "M": M, "N": N, "K": K, "epi": epi, "us": round(us, 2),
+            "weight_TBps": round(N * K * 2 / us / 1e6, 3), "TFLOPS": round(2 * M * N * K / us / 1e6, 1)}
+
+
+def _decode_meta(B: int, L: int, PS: int = 256):
+    from ..ops.attention import AttnMeta
+
+    npg = -(-L // PS)
+    i32 = lambda v: torch.tensor(v, dtype=torch.int32, device="cuda")  # noqa: E731
+    return AttnMeta(qo_indptr=i32(list(range(B + 1))), positions=i32([L - 1] * B),
+                    seg_indptr=i32(list(range(B + 1))), seg_page_indptr=i32([i * npg for i in range(B + 1)]),
+                    seg_offset=i32([0] * B), seg_len=i32([L] * B), seg_pos0=i32([0] * B), seg_delta=i32([0] * B),
+                    page_ids=i32(list(range(B * npg))), num_seqs=B, max_q_len=1, max_kv_len=L, decode=True), npg
+
+
+def bench_attn_decode(B: int, L: int, Hq: int, Hkv: int, splits: int = 0, D: int = 128) -> dict:
+    from .. import ops
+
+    meta, npg = _decode_meta(B, L)
+    kv = torch.randn(B * npg + 1, 2, Hkv, 256, D, device="cuda").bfloat16()
+    q = torch.randn(B, Hq, D, device="cuda").bfloat16()
+    cos, sin = ops.build_cos_sin(D, 500000.0, 2 * L + 16, device="cuda")
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    meta.num_splits = splits or max(1, min(32, (2 * sms) // (B * Hkv)))
+    us = _graph_time(lambda: ops.attention(q, kv, meta, cos, sin, D ** -0.5))
+    byts = B * L * Hkv * D * 2 * 2
+    return {"kernel": "attn_decode", "B": B, "L": L, "Hq": Hq, "Hkv": Hkv, "splits": meta.num_splits,
+            "us": round(us, 2), "kv_TBps": round(byts / us / 1e6, 3)}
+
+
+def bench_attn_prefill(L: int, Hq: int, Hkv: int, B: int = 1, D: int = 128) -> dict:
+    from .. import ops
+    from ..ops.attention import AttnMeta
+
+    PS = 256
+    npg = -(-L // PS)
+    i32 = lambda v: torch.tensor(v, dtype=torch.int32, device="cuda")  # noqa: E731
+    meta = AttnMeta(qo_indptr=i32([i * L for i in range(B + 1)]), positions=i32(list(range(L)) * B),
+                    seg_indptr=i32(list(range(B + 1))), seg_page_indptr=i32([i * npg for i in range(B + 1)]),
+                    seg_offset=i32([0] * B), seg_len=i32([L] * B), seg_pos0=i32([0] * B), seg_delta=i32([0] * B),
+                    page_ids=i32(list(range(B * npg))), num_seqs=B, max_q_len=L, max_kv_len=L, decode=False)
+    kv = torch.randn(B * npg + 1, 2, Hkv, PS, D, device="cuda").bfloat16()
+    q = torch.randn(B * L, Hq, D, device="cuda").bfloat16()
+    cos, sin = ops.build_cos_sin(D, 500000.0, 2 * L + 16, device="cuda")
+    us = _eager_time(lambda: ops.attention(q, kv, meta, cos, sin, D ** -0.5))
+    flops = B * 4 * L * L / 2 * Hq * D
+    return {"kernel": "attn_prefill", "L": L, "Hq": Hq, "Hkv": Hkv, "B": B, "us": round(us, 1),
+            "TFLOPS_causal": round(flops / us / 1e6, 1)}
+
+
+def decode_step(model: str, B: int, plen: int) -> None:
+    import os
+    import tempfile
+
+    from .. import LLM, SamplingParams
+    from .synthetic import make_checkpoint
+
+    d = os.path.join(tempfile.gettempdir(), f"braid_mb_{model}")
+    if not os.path.exists(os.path.join(d, "config.json")):
+        make_checkpoint(d, model, write_weights=False)
+    page = 256
+    llm = LLM(d, load_weights=False, max_num_seqs=B, max_model_len=plen + 64,
+              num_kvcache_blocks=B * math.ceil((plen + 64) / page) + 8, enforce_eager=True,
+              max_num_batched_tokens=max(16384, plen + 64))
+    g = torch.Generator().manual_seed(3)
+    for _ in range(B):
+        llm.add_request(torch.randint(3, llm.config.spec.vocab_size, (plen,), generator=g).tolist(),
+                        SamplingParams(temperature=0, max_tokens=16, ignore_eos=True))
+    while llm.scheduler.waiting:
+        llm.step()
+    for _ in range(3):
+        llm.step()
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStart()
+    llm.step()
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStop()
+
+
+def main(argv=None) -> None:
+    import json
+
+    ap = argparse.ArgumentParser()
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    g = sub.add_parser("gemm")
+    g.add_argument("M", type=int), g.add_argument("N", type=int), g.add_argument("K", type=int)
+    g.add_argument("--epi", type=int, default=0)
+    g.add_argument("--graph", action="store_true")
+    a = sub.add_parser("attn-decode")
+    for n in ("B", "L", "Hq", "Hkv"):
+        a.add_argument(n, type=int)
+    a.add_argument("--splits", type=int, default=0)
+    p = sub.add_parser("attn-prefill")
+    for n in ("L", "Hq", "Hkv"):
+        p.add_argument(n, type=int)
+    p.add_argument("--batch", type=int, default=1)
+    s = sub.add_parser("decode-step")
+    s.add_argument("model"), s.add_argument("B", type=int), s.add_argument("plen", type=int)
+    args = ap.parse_args(argv)
+    if args.cmd == "gemm":
+        print(json.dumps(bench_gemm(args.M, args.N, args.K, args.epi, args.graph)))
+    elif args.cmd == "attn-decode":
+        print(json.dumps(bench_attn_decode(args.B, args.L, args.Hq, args.Hkv, args.splits)))
+    elif args.cmd == "attn-prefill":
+        print(json.dumps(bench_attn_prefill(args.L, args.Hq, args.Hkv, args.batch)))
+    else:
+        decode_step(args.model, args.B, args.plen)
+        print("decode step done")
+
+
+if __name__ == "__main__":
+    main()

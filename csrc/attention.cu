@@ -550,14 +550,33 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(const __grid_consta
 }
 
 // -------------------------------------------------------------- prefill
-template <int D>
-__global__ void __launch_bounds__(128) attn_prefill_kernel(const AttnParams p) {
-  extern __shared__ __align__(128) uint8_t sm[];
-  uint8_t* qs = sm;                                  // [64][D]
-  uint8_t* kbuf = sm + 64 * D * 2;                   // 2 x [64][D]
-  uint8_t* vbuf = kbuf + 2 * KT * D * 2;
+// Prefill (or chunk self-prefill) attention: grid (64-row q tile, seq, kv
+// head); rows are (token, head-in-group) pairs.  Warp 0 streams 64-key K/V
+// tiles with TMA into a STAGES-deep mbarrier ring (as in decode) while each
+// warp computes its 16 rows against every tile; tiles past the last query
+// position of this q tile are not loaded.
+template <int D, int STAGES, int BR>
+__global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const __grid_constant__ CUtensorMap tmkv,
+                                                              const AttnParams p) {
+  constexpr int TILE = KT * D * 2;
+  extern __shared__ uint8_t sm_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* kbuf = sm;
+  uint8_t* vbuf = sm + STAGES * TILE;
+  uint8_t* qs = vbuf + STAGES * TILE;  // [64][D], tswz<64>
+  uint64_t* full = reinterpret_cast<uint64_t*>(qs + 64 * D * 2);
+  uint64_t* empty = full + STAGES;
   const int b = blockIdx.y, kh = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmkv);
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 4);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
   pdl_wait();
   pdl_trigger();
   const int G = p.G;
@@ -568,12 +587,6 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const AttnParams p) {
   const int nrows = min(64, rows - row0);
   const int max_pos = p.positions[t0 + (row0 + nrows - 1) / G];
   const int min_pos = p.positions[t0 + row0 / G];
-  auto row_tok = [&](int r, int& tok, int& g) {
-    const int rr = row0 + r;
-    tok = t0 + rr / G;
-    g = rr % G;
-  };
-  // positions of this thread's two rows (g and g+8 of the warp's slab)
   const int gq = lane >> 2;
   int rpos[2];
 #pragma unroll
@@ -581,46 +594,160 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const AttnParams p) {
     const int rr = row0 + warp * 16 + gq + 8 * h;
     rpos[h] = rr < rows ? p.positions[t0 + rr / G] : -1;
   }
+  const int s0 = p.seg_indptr[b], s1 = p.seg_indptr[b + 1];
+  // restrict each segment to keys that some row of this tile can see
+  ProdCursor pc{s0, s1, 0, 0, 0, 0, 0, 0, 0, 0, nullptr};
+  auto seg_hi = [&](int s, int len) { return min(len, max_pos - p.seg_pos0[s] + 1); };
+  auto settle = [&]() {
+    while (pc.s < pc.s1) {
+      const int len = p.seg_len[pc.s];
+      pc.lo = 0;
+      pc.hi = seg_hi(pc.s, len);
+      if (pc.hi > 0) {
+        pc.off = p.seg_offset[pc.s];
+        pc.pages = p.page_ids + p.seg_page_indptr[pc.s];
+        pc.npages = p.seg_page_indptr[pc.s + 1] - p.seg_page_indptr[pc.s];
+        pc.sl = pc.off & ~(KT - 1);
+        pc.win = -(1 << 30);
+        return;
+      }
+      ++pc.s;
+    }
+  };
+  auto advance = [&]() {
+    pc.sl += KT;
+    if (pc.sl < pc.off + pc.hi) return;
+    ++pc.s;
+    settle();
+  };
+  auto issue = [&](int st) {
+#pragma unroll
+    for (int q = 0; q < KT / BR; ++q) {
+      const int slot = pc.sl + q * BR;
+      const int pidx = min(slot / p.PS, pc.npages - 1);
+      if (pidx < pc.win || pidx >= pc.win + 32) {
+        pc.win = pidx;
+        pc.win_page = pc.win + lane < pc.npages ? pc.pages[pc.win + lane] : 0;
+      }
+      const int page = __shfl_sync(0xffffffffu, pc.win_page, pidx - pc.win);
+      if (lane == 0) {
+        const int row_k = ((page * 2 + 0) * p.Hkv + kh) * p.PS + slot % p.PS;
+        const int row_v = row_k + p.Hkv * p.PS;
+#pragma unroll
+        for (int h = 0; h < D / 64; ++h) {
+          tma_load_2d(kbuf + st * TILE + h * (KT * 128) + q * BR * 128, &tmkv, &full[st], h * 64, row_k);
+          tma_load_2d(vbuf + st * TILE + h * (KT * 128) + q * BR * 128, &tmkv, &full[st], h * 64, row_v);
+        }
+      }
+    }
+  };
+  int issued = 0;
+  if (warp == 0) {
+    settle();
+    for (; issued < STAGES - 1 && pc.s < pc.s1; ++issued) {
+      if (lane == 0) mbar_arrive_expect_tx(&full[issued], 2 * TILE);
+      issue(issued);
+      advance();
+    }
+  }
 
   float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
   float acc[D / 8][4];
 #pragma unroll
   for (int i = 0; i < D / 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
   uint32_t qf[D / 16][4];
-
-  const int s0 = p.seg_indptr[b], s1 = p.seg_indptr[b + 1];
+  int it = 0;
+  bool ok = true;
+  // every warp runs the same segment iterations (and so the same barriers),
+  // even after a timed-out wait has stopped its tile loop
   for (int s = s0; s < s1; ++s) {
+    const int len = p.seg_len[s];
     const int pos0 = p.seg_pos0[s];
-    const int hi = min(p.seg_len[s], max_pos - pos0 + 1);
+    const int hi = seg_hi(s, len);
     if (hi <= 0) continue;
     __syncthreads();
-    build_q_tile<D>(p, kh, p.seg_delta[s], nrows, 64, qs, row_tok);
-    load_kv_tile<D>(p, s, kh, 0, hi, kbuf, vbuf);
-    cp_async_commit();
-    __syncthreads();
-    load_q_frags<D>(qs, warp * 16, qf);
-    int buf = 0;
-    for (int j0 = 0; j0 < hi; j0 += KT) {
-      if (j0 + KT < hi) {
-        load_kv_tile<D>(p, s, kh, j0 + KT, hi, kbuf + (buf ^ 1) * KT * D * 2, vbuf + (buf ^ 1) * KT * D * 2);
-        cp_async_commit();
-        cp_async_wait<1>();
-      } else {
-        cp_async_wait<0>();
+    {
+      constexpr int H2 = D / 2;
+      const int delta = p.seg_delta[s];
+      __nv_bfloat16* qt = reinterpret_cast<__nv_bfloat16*>(qs);
+#pragma unroll 4
+      for (int k = 0; k < 64 * H2 / 128; ++k) {
+        const int i = threadIdx.x + 128 * k;
+        const int r = i / H2, d = i % H2;
+        float x1 = 0.f, x2 = 0.f;
+        if (r < nrows) {
+          const int rr = row0 + r;
+          const int tok = t0 + rr / G, g = rr % G;
+          const __nv_bfloat16* qp = p.q + ((size_t)tok * p.Hq + kh * G + g) * D;
+          const float a = bf2f(qp[d]), bb = bf2f(qp[d + H2]);
+          if (p.use_rope) {
+            int pos = p.positions[tok] - delta;
+            pos = pos < 0 ? 0 : (pos >= p.rope_len ? p.rope_len - 1 : pos);
+            const float cs = p.cos[(size_t)pos * H2 + d], sn = p.sin[(size_t)pos * H2 + d];
+            x1 = a * cs - bb * sn;
+            x2 = bb * cs + a * sn;
+          } else {
+            x1 = a;
+            x2 = bb;
+          }
+        }
+        qt[(tswz<64>(r, d / 8) >> 1) + (d & 7)] = f2bf(x1);
+        qt[(tswz<64>(r, (d + H2) / 8) >> 1) + ((d + H2) & 7)] = f2bf(x2);
       }
-      __syncthreads();
-      const uint8_t* ks = kbuf + buf * KT * D * 2;
-      const uint8_t* vs = vbuf + buf * KT * D * 2;
+    }
+    __syncthreads();
+    {
+      const int r = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk)
+        ldsm_x4(smem_u32(qs) + tswz<64>(r, kk * 2 + (lane >> 4)), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+    }
+    const int off = p.seg_offset[s];
+    for (int sl = off & ~(KT - 1); sl < off + hi && ok; sl += KT, ++it) {
+      if (warp == 0 && pc.s < pc.s1) {
+        const int st2 = issued % STAGES;
+        int okw = 1;
+        if (lane == 0) {
+          if (issued >= STAGES) okw = mbar_wait(&empty[st2], ((issued / STAGES) & 1) ^ 1) ? 1 : 0;
+          if (okw) mbar_arrive_expect_tx(&full[st2], 2 * TILE);
+        }
+        if (__shfl_sync(0xffffffffu, okw, 0)) {
+          issue(st2);
+          advance();
+          ++issued;
+        } else {
+          pc.s = pc.s1;
+        }
+      }
+      const int st = it % STAGES;
+      if (!mbar_wait(&full[st], (it / STAGES) & 1)) {
+        ok = false;
+        break;
+      }
+      const uint8_t* ks = kbuf + st * TILE;
+      const uint8_t* vs = vbuf + st * TILE;
       float sc[8][4];
-      qk_tile<D, 8>(qf, ks, 0, sc);
-      const bool need_mask = (pos0 + j0 + KT - 1 > min_pos) || (j0 + KT > hi);
+#pragma unroll
+      for (int nb = 0; nb < 8; ++nb) {
+        sc[nb][0] = sc[nb][1] = sc[nb][2] = sc[nb][3] = 0.f;
+        const int row = nb * 8 + (lane & 7);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; kk += 2) {
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(smem_u32(ks) + tswz<KT>(row, kk * 2 + (lane >> 3)), b0, b1, b2, b3);
+          mma16816(sc[nb], qf[kk], b0, b1);
+          mma16816(sc[nb], qf[kk + 1], b2, b3);
+        }
+      }
+      const int j0 = sl - off;
+      const bool need_mask = (pos0 + j0 + KT - 1 > min_pos) || j0 < 0 || (j0 + KT > hi);
       if (need_mask) {
 #pragma unroll
         for (int nb = 0; nb < 8; ++nb)
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int j = j0 + nb * 8 + 2 * (lane & 3) + (e & 1);
-            const bool vis = j < hi && pos0 + j <= rpos[e >> 1];
+            const bool vis = j >= 0 && j < hi && pos0 + j <= rpos[e >> 1];
             sc[nb][e] = vis ? sc[nb][e] * p.scale_log2 : -INFINITY;
           }
       } else {
@@ -630,9 +757,24 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const AttnParams p) {
           for (int e = 0; e < 4; ++e) sc[nb][e] *= p.scale_log2;
       }
       softmax_update<8, D>(sc, m, l, acc);
-      pv_tile<D, 4>(sc, vs, 0, acc);
-      __syncthreads();
-      buf ^= 1;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint32_t a[4];
+        a[0] = pack_bf16(sc[2 * j][0], sc[2 * j][1]);
+        a[1] = pack_bf16(sc[2 * j][2], sc[2 * j][3]);
+        a[2] = pack_bf16(sc[2 * j + 1][0], sc[2 * j + 1][1]);
+        a[3] = pack_bf16(sc[2 * j + 1][2], sc[2 * j + 1][3]);
+        const int row = j * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+        for (int nb = 0; nb < D / 8; nb += 2) {
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4_t(smem_u32(vs) + tswz<KT>(row, nb + (lane >> 4)), b0, b1, b2, b3);
+          mma16816(acc[nb], a, b0, b1);
+          mma16816(acc[nb + 1], a, b2, b3);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
     }
   }
   // ---- normalise and store
@@ -704,15 +846,29 @@ static void launch_attn(AttnParams& p, int num_seqs, int max_q_len, bool decode,
       launch_pdl(k, dim3(num_seqs, p.Hkv, p.num_splits), dim3(128), smem, st, tm, p);
     }
   } else {
-    const int smem = 64 * D * 2 + 4 * KT * D * 2;
-    auto k = attn_prefill_kernel<D>;
-    static bool attr = false;
-    if (!attr) {
-      C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      attr = true;
-    }
+    constexpr int STAGES = D == 128 ? 2 : 3;
+    const int smem = 2 * STAGES * KT * D * 2 + 64 * D * 2 + 2 * STAGES * 8 + 1024;
+    const int64_t rows = P * 2 * p.Hkv * p.PS;
     const int qt = (max_q_len * p.G + 63) / 64;
-    launch_pdl(k, dim3(qt, num_seqs, p.Hkv), dim3(128), smem, st, p);
+    if (p.PS % 64 == 0) {
+      auto k = attn_prefill_kernel<D, STAGES, 64>;
+      static bool attr = false;
+      if (!attr) {
+        C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        attr = true;
+      }
+      CUtensorMap tm = make_tmap(p.kv, rows, D, D, 64);
+      launch_pdl(k, dim3(qt, num_seqs, p.Hkv), dim3(128), smem, st, tm, p);
+    } else {
+      auto k = attn_prefill_kernel<D, STAGES, 16>;
+      static bool attr = false;
+      if (!attr) {
+        C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        attr = true;
+      }
+      CUtensorMap tm = make_tmap(p.kv, rows, D, D, 16);
+      launch_pdl(k, dim3(qt, num_seqs, p.Hkv), dim3(128), smem, st, tm, p);
+    }
   }
 }
 

@@ -106,6 +106,13 @@ BRAID_DEVICE float4 dsmem_ld_f4(uint32_t addr) {
 // cumulative over the writes the barrier ordered before it (release side);
 // before a CTA barrier it orders the other threads' later reads (acquire side).
 BRAID_DEVICE void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+// atomicAdd with acquire-release semantics at GPU scope (release is cumulative
+// over writes ordered before it by a CTA barrier).
+BRAID_DEVICE int atomic_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
 
 BRAID_DEVICE void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");

@@ -334,13 +334,10 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
       }
       named_bar_sync(1, 128);
       if (et == 0) {
-        fence_acq_rel_gpu();  // release this CTA's partial (cumulative over the barrier)
-        const int old = atomicAdd(&args.counters[tile], 1);
+        // releases this CTA's partial, acquires the other slices' partials
+        const int old = atomic_add_acq_rel_gpu(&args.counters[tile], 1);
         *s_flag = (old == args.splits - 1);
-        if (old == args.splits - 1) {
-          args.counters[tile] = 0;
-          fence_acq_rel_gpu();  // acquire the other slices' partials
-        }
+        if (old == args.splits - 1) args.counters[tile] = 0;
       }
       named_bar_sync(1, 128);
       last = *s_flag != 0;
@@ -419,15 +416,36 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
           if (!args.swap) {
             const int m = m0 + r;
             if (m < args.M) {
-              __nv_bfloat16* o = args.out + (size_t)m * args.ldo;
-              const __nv_bfloat16* res = args.residual ? args.residual + (size_t)m * args.ldr : nullptr;
+              __nv_bfloat16* o = args.out + (size_t)m * args.ldo + n0 + c0;
+              const __nv_bfloat16* res = args.residual ? args.residual + (size_t)m * args.ldr + n0 + c0 : nullptr;
+              const bool vec = n0 + c0 + 16 <= args.N && ((reinterpret_cast<uintptr_t>(o) |
+                               reinterpret_cast<uintptr_t>(res)) & 15) == 0;
+              if (vec) {
+                // 16 outputs = two 16-byte stores (the row is this thread's)
+                uint4 rv[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+                if (res) {
+                  rv[0] = *reinterpret_cast<const uint4*>(res);
+                  rv[1] = *reinterpret_cast<const uint4*>(res + 8);
+                }
+                const __nv_bfloat16* re = reinterpret_cast<const __nv_bfloat16*>(rv);
+                uint4 ov[2];
+                __nv_bfloat16* oe = reinterpret_cast<__nv_bfloat16*>(ov);
 #pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                const int n = n0 + c0 + j;
-                if (n < args.N) {
+                for (int j = 0; j < 16; ++j) {
                   float y = rbf(v[j]);
-                  if (res) y += bf2f(res[n]);
-                  o[n] = f2bf(y);
+                  if (res) y += bf2f(re[j]);
+                  oe[j] = f2bf(y);
+                }
+                *reinterpret_cast<uint4*>(o) = ov[0];
+                *reinterpret_cast<uint4*>(o + 8) = ov[1];
+              } else {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                  if (n0 + c0 + j < args.N) {
+                    float y = rbf(v[j]);
+                    if (res) y += bf2f(res[j]);
+                    o[j] = f2bf(y);
+                  }
                 }
               }
             }
@@ -483,14 +501,22 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
             load_cols(blk * 128 + c0, g);
             load_cols(blk * 128 + 64 + c0, u);
             if (m < args.M) {
+              const int f0 = (n0 + blk * 128) / 2 + c0;
+              __nv_bfloat16* o = args.out + (size_t)m * args.ldo + f0;
+              uint4 ov[2];
+              __nv_bfloat16* oe = reinterpret_cast<__nv_bfloat16*>(ov);
 #pragma unroll
               for (int j = 0; j < 16; ++j) {
-                const int f = (n0 + blk * 128) / 2 + c0 + j;
-                if (2 * f < args.N) {
-                  const float gg = rbf(g[j]), uu = rbf(u[j]);
-                  const float sg = rbf(gg / (1.f + __expf(-gg)));
-                  args.out[(size_t)m * args.ldo + f] = f2bf(sg * uu);
-                }
+                const float gg = rbf(g[j]), uu = rbf(u[j]);
+                const float sg = rbf(gg / (1.f + __expf(-gg)));
+                oe[j] = f2bf(sg * uu);
+              }
+              if (2 * (f0 + 16) <= args.N && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+                *reinterpret_cast<uint4*>(o) = ov[0];
+                *reinterpret_cast<uint4*>(o + 8) = ov[1];
+              } else {
+                for (int j = 0; j < 16; ++j)
+                  if (2 * (f0 + j) < args.N) o[j] = oe[j];
               }
             }
           }
@@ -592,6 +618,9 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
             float a[16], b[16];
             load_cols(col0 + c, a);
             load_cols(col0 + D / 2 + c, b);
+            uint4 w1[2], w2[2];
+            __nv_bfloat16* e1 = reinterpret_cast<__nv_bfloat16*>(w1);
+            __nv_bfloat16* e2 = reinterpret_cast<__nv_bfloat16*>(w2);
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
               float x1 = rbf(a[j]), x2 = rbf(b[j]);
@@ -605,9 +634,14 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
                 x1 = y1;
                 x2 = y2;
               }
-              dst[c + j] = f2bf(x1);
-              dst[D / 2 + c + j] = f2bf(x2);
+              e1[j] = f2bf(x1);
+              e2[j] = f2bf(x2);
             }
+            // head rows are 16-byte aligned (D and c are multiples of 8)
+            *reinterpret_cast<uint4*>(dst + c) = w1[0];
+            *reinterpret_cast<uint4*>(dst + c + 8) = w1[1];
+            *reinterpret_cast<uint4*>(dst + D / 2 + c) = w2[0];
+            *reinterpret_cast<uint4*>(dst + D / 2 + c + 8) = w2[1];
           }
         }
       }
