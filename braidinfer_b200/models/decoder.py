@@ -240,6 +240,9 @@ class DecoderLM:
         S, L = self.spec, self.layout
         assert self.finalized, "call finalize() after loading weights"
         eps = S.rms_norm_eps
+        fc = comm.get_fused_comm() if self.tp.size > 1 else None
+        if fc is not None and input_ids.is_cuda and fc.can_sp(input_ids.shape[0]):
+            return self._forward_sp(fc, input_ids, positions, slot_mapping, meta, kv_cache, workspace)
         residual = self.embed_tokens(input_ids, positions)
         for i, w in enumerate(self.layers):
             q = ops.qkv_gemm(residual, w.qkv_w, w.qkv_b, eps, positions, slot_mapping, kv_cache[i], L.q_heads,
@@ -249,6 +252,35 @@ class DecoderLM:
             g = ops.linear_swiglu(residual, w.gu_w, rms_eps=eps)
             residual = self._row_parallel(g, w.down_w, residual)
         return residual
+
+    def _forward_sp(self, fc, input_ids, positions, slot_mapping, meta, kv_cache, workspace) -> torch.Tensor:
+        """Tensor-parallel prefill, sequence-parallel residual stream.
+
+        The residual ``G`` lives in the peer-mapped comm buffer.  Per layer:
+        QKV GEMM (waits tile by tile for gathered rows, 1/rms pushed with them)
+        → attention → o_proj GEMM → reduce-scatter in its epilogue → owner
+        reduce + all-gather of rows and 1/rms → gate/up GEMM (same waits) →
+        down GEMM → reduce-scatter → reduce + all-gather.  Replaces the
+        all-reduce that the reference's ``RowParallelLinear`` never issued
+        (``braidinfer/layers/linear_distributed.py:170-174``).
+        """
+        S, L = self.spec, self.layout
+        eps = S.rms_norm_eps
+        G, rstd = fc.sp_begin(input_ids.shape[0])
+        ops.embedding(input_ids, self.embed, 0, out=G)
+        ops.row_rstd(G, eps, rstd)
+        for i, w in enumerate(self.layers):
+            q = ops.qkv_gemm(G, w.qkv_w, w.qkv_b, eps, positions, slot_mapping, kv_cache[i], L.q_heads,
+                             L.kv_heads, S.head_dim, self.cos, self.sin, w.q_norm, w.k_norm, eps, S.use_rope,
+                             rs_vec=rstd, sp=fc.sp_params())
+            o = ops.attention(q, kv_cache[i], meta, self.cos, self.sin, self.scale, S.use_rope, workspace)
+            fc.sp_linear_reduce_scatter(o.view(o.shape[0], -1), w.o_w, G)
+            fc.sp_reduce_allgather(eps)
+            g = ops.linear_swiglu(G, w.gu_w, rms_eps=eps, rs_vec=rstd, sp=fc.sp_params())
+            fc.sp_linear_reduce_scatter(g, w.down_w, G)
+            fc.sp_reduce_allgather(eps)
+        fc.sp_wait()
+        return G.clone()
 
     def _row_parallel(self, x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor) -> torch.Tensor:
         """``residual += x @ w.T`` summed over tensor-parallel ranks."""

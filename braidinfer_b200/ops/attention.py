@@ -93,16 +93,19 @@ def qkv_gemm(x: torch.Tensor, w_qkv: torch.Tensor, bias: Optional[torch.Tensor],
              positions: torch.Tensor, slot_mapping: torch.Tensor, kv_layer: torch.Tensor, num_q_heads: int,
              num_kv_heads: int, head_dim: int, cos: torch.Tensor, sin: torch.Tensor,
              q_norm: Optional[torch.Tensor] = None, k_norm: Optional[torch.Tensor] = None, eps: float = 1e-6,
-             use_rope: bool = True) -> torch.Tensor:
+             use_rope: bool = True, rs_vec: Optional[torch.Tensor] = None,
+             sp: Optional[torch.Tensor] = None) -> torch.Tensor:
     """QKV projection (fused input RMSNorm when ``rms_eps`` is set, norm weight
     folded into ``w_qkv``) with the q/k-norm, RoPE(k) and paged KV append done
-    in the GEMM epilogue on CUDA.  Returns unrotated q ``[T, Hq, D]``."""
+    in the GEMM epilogue on CUDA.  Returns unrotated q ``[T, Hq, D]``.
+    ``rs_vec``/``sp``: precomputed ``1/rms`` and sequence-parallel parameters
+    (CUDA tensor-parallel prefill)."""
     T = x.shape[0]
     if x.is_cuda:
         q = torch.empty(T, num_q_heads, head_dim, dtype=x.dtype, device=x.device)
         ext().gemm_qkv(q, x, w_qkv, bias, -1.0 if rms_eps is None else float(rms_eps), positions, slot_mapping,
                        kv_layer, q_norm, k_norm, float(eps), cos, sin, num_q_heads, num_kv_heads, head_dim,
-                       bool(use_rope))
+                       bool(use_rope), rs_vec, sp)
         return q
     from .linear import linear
 

@@ -87,12 +87,16 @@ def swiglu_ref_from_interleaved(y: torch.Tensor, dtype: torch.dtype, block: int 
 
 
 def linear_swiglu(x: torch.Tensor, w_gu: torch.Tensor, out: Optional[torch.Tensor] = None,
-                  rms_eps: Optional[float] = None) -> torch.Tensor:
-    """``silu(x @ Wg.T) * (x @ Wu.T)`` from the block-interleaved ``w_gu``."""
+                  rms_eps: Optional[float] = None, rs_vec: Optional[torch.Tensor] = None,
+                  sp: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``silu(x @ Wg.T) * (x @ Wu.T)`` from the block-interleaved ``w_gu``.
+
+    ``rs_vec`` (CUDA only) supplies each token's precomputed ``1/rms``; ``sp`` is
+    the sequence-parallel parameter block (the GEMM waits for gathered rows)."""
     if x.is_cuda:
         M = x.shape[0]
         out = torch.empty(M, w_gu.shape[0] // 2, dtype=x.dtype, device=x.device) if out is None else out
-        ext().gemm(out, x, w_gu, None, None, 1, -1.0 if rms_eps is None else float(rms_eps))
+        ext().gemm(out, x, w_gu, None, None, 1, -1.0 if rms_eps is None else float(rms_eps), rs_vec, sp)
         return out
     y = _acc(x, w_gu, None, rms_eps)
     r = swiglu_ref_from_interleaved(y, x.dtype)

@@ -49,3 +49,14 @@ def layer_norm(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float) ->
         ext().layer_norm(out, x, w, b, float(eps))
         return out
     return torch.nn.functional.layer_norm(x.float(), (x.shape[-1],), w.float(), b.float(), eps).to(x.dtype)
+
+
+def row_rstd(x: torch.Tensor, eps: float, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``1/rms`` of each row of ``x`` in fp32 (the scale a fused-norm GEMM applies)."""
+    if out is None:
+        out = torch.empty(x.shape[0], dtype=torch.float32, device=x.device)
+    if x.is_cuda:
+        ext().row_rstd(x, float(eps), out)
+        return out
+    out.copy_(torch.rsqrt(x.float().pow(2).mean(-1) + eps))
+    return out

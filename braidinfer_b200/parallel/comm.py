@@ -2,7 +2,7 @@
 
 ``nccl`` backend: plain ``torch.distributed`` calls — the baseline.
 ``fused`` backend: the all-reduce of row-parallel GEMM outputs is done by the
-native one-shot push kernel over peer memory (``csrc/comm_kernels.cu``) when the
+native one-shot push kernel over peer memory (``csrc/comm.cu``) when the
 symmetric workspace is available; otherwise it falls back to NCCL with a log
 line, never silently on a GPU box where the workspace was requested.
 """

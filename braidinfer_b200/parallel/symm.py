@@ -12,6 +12,23 @@ peer memory over NVLink (``csrc/comm.cu``, ``csrc/gemm_tcgen05.cu`` epi 3):
   sources, sums in fp32 and adds the residual.  One NVLink hop, no NCCL call.
 * ``all_reduce(x)``: the same protocol for a tensor computed elsewhere.
 
+Prefill-sized batches (``maxT < T <= sp_max_tokens``) run sequence-parallel:
+token rows are owned by ranks in blocks of ``ceil(T / tp)`` and the residual
+stream lives in a gathered buffer ``G [T, hidden]`` inside the comm buffer.
+
+* ``sp_linear_reduce_scatter(x, w)``: o_proj / down_proj GEMM whose epilogue
+  stores each output row straight into its owner's receive slot (GEMM →
+  reduce-scatter in one kernel; each rank sends ``(tp-1)/tp`` of its partial).
+* ``sp_reduce_allgather(eps)``: the owner sums the partials, adds the residual,
+  computes the row's ``1/rms`` and stores row + ``1/rms`` into every rank's
+  ``G`` (all-gather by peer stores).
+* the next QKV / gate_up GEMM (input RMSNorm fused) waits per 128-row tile
+  for that tile's owners and then TMA-loads ``G`` locally (all-gather → GEMM);
+  tiles whose rows have arrived run while others are still in flight.
+
+Counters are cumulative; the expected values are tracked here on the host,
+so these prefill calls are never captured in a CUDA graph.
+
 Every wait is bounded (``comm_timeout_s``); an expired wait leaves a status
 word that :meth:`FusedComm.check` turns into ``CommTimeoutError``.  No NVLS
 multicast object and no TMA load of peer memory is used.  The NCCL path stays
@@ -33,7 +50,7 @@ log = get_logger("symm")
 
 class FusedComm:
     def __init__(self, tp: TPState, hidden: int, device: torch.device, max_tokens: int = 64,
-                 timeout_s: float = 5.0):
+                 timeout_s: float = 5.0, sp_max_tokens: int = 0):
         from ..ops._ext import ext
 
         self.tp = tp
@@ -43,9 +60,30 @@ class FusedComm:
         self.timeout_s = timeout_s
         self._C = ext()
         dev = device.index
+
+        def align(n: int) -> int:
+            return (n + 255) // 256 * 256
+
         data = 2 * tp.size * max_tokens * hidden * 2
-        self.flags_off = (data + 255) // 256 * 256
-        nbytes = self.flags_off + 8 * tp.size + 256
+        self.flags_off = align(data)
+        off = self.flags_off + align(8 * tp.size)
+        # sequence-parallel prefill region
+        self.sp_max = sp_max_tokens if sp_max_tokens > max_tokens else 0
+        self.rs_flags_off = off
+        off += align(8 * tp.size)
+        self.ag_flags_off = off
+        off += align(8 * tp.size)
+        self.g_off = off
+        off += align(self.sp_max * hidden * 2)
+        self.rstd_off = off
+        off += align(self.sp_max * 4)
+        self.recv_off = off
+        off += align(tp.size * (-(-self.sp_max // tp.size)) * hidden * 2)
+        nbytes = off + 256
+        self.sp_rs_expected = 0
+        self.sp_ag_expected = 0
+        self.sp_T = 0
+        self.sp_rpr = 0
         ptr, handle = self._C.comm_alloc(nbytes, dev)
         self.local_ptr = int(ptr.item())
         handles = [None] * tp.size
@@ -75,9 +113,48 @@ class FusedComm:
         st = self.status.tolist()
         if st[0] != 0:
             self.status.zero_()
+            what = {1: "all-reduce", 2: "all-gather", 3: "reduce-scatter"}.get(st[0], "collective")
             raise CommTimeoutError(
-                f"rank {st[1]} timed out after {self.timeout_s}s waiting for rank {st[2]} (all-reduce #{st[3]})",
+                f"rank {st[1]} timed out after {self.timeout_s}s waiting for rank {st[2]} ({what} #{st[3]})",
                 {"code": st[0], "rank": st[1], "peer": st[2], "epoch": st[3]})
+
+    # ------------------------------------------ sequence-parallel prefill
+    def can_sp(self, T: int) -> bool:
+        return self.maxT < T <= self.sp_max
+
+    def sp_begin(self, T: int):
+        """Start a sequence-parallel forward of ``T`` tokens; returns views of
+        the gathered residual ``G [T, H]`` and its per-row ``1/rms [T]``."""
+        assert self.can_sp(T)
+        self.sp_T = T
+        self.sp_rpr = -(-T // self.tp.size)
+        dev = self.device.index
+        G = self._C.comm_tensor(self.local_ptr, self.g_off, [T, self.H], 0, dev)
+        rstd = self._C.comm_tensor(self.local_ptr, self.rstd_off, [T], 1, dev)
+        return G, rstd
+
+    def sp_params(self, wait: bool = True) -> torch.Tensor:
+        """Parameter block of the GEMM's sequence-parallel mode (CPU int64)."""
+        return torch.tensor([self.peers.data_ptr(), self.recv_off, self.rs_flags_off, self.ag_flags_off,
+                             self.sp_ag_expected if wait else 0, self.status.data_ptr(),
+                             int(self.timeout_s * 1e9), self.tp.rank, self.tp.size, self.sp_rpr, self.H],
+                            dtype=torch.int64)
+
+    def sp_linear_reduce_scatter(self, x: torch.Tensor, w: torch.Tensor, G: torch.Tensor) -> None:
+        """Row-parallel GEMM whose epilogue pushes each row to its owner."""
+        n = self._C.gemm(G, x, w, None, None, 4, -1.0, None, self.sp_params(wait=False))
+        self.sp_rs_expected += int(n)
+
+    def sp_reduce_allgather(self, eps: float) -> None:
+        n = self._C.sp_reduce_allgather(self.peers, self.recv_off, self.rs_flags_off, self.ag_flags_off, self.g_off,
+                                        self.rstd_off, self.tp.rank, self.tp.size, self.sp_rpr, self.sp_T, self.H,
+                                        self.sp_rs_expected, float(eps), self.status, self.timeout_s)
+        self.sp_ag_expected += int(n)
+
+    def sp_wait(self) -> None:
+        """Make all of ``G`` readable by ordinary kernels later on the stream."""
+        self._C.sp_wait(self.local_ptr, self.ag_flags_off, self.tp.size, self.tp.rank, self.sp_ag_expected,
+                        self.status, self.timeout_s)
 
     # -------------------------------------------------------- collectives
     def _reduce(self, out: torch.Tensor, residual: Optional[torch.Tensor], arrivals: int) -> torch.Tensor:
@@ -129,7 +206,9 @@ class FusedComm:
 
 def maybe_enable_fused_comm(config, runner) -> Optional[FusedComm]:
     """Create the peer-memory runtime for this TP group and route the model's
-    collectives through it (decode shapes); prefill-sized tensors use NCCL."""
+    collectives through it: one-shot push all-reduce for decode shapes,
+    sequence-parallel reduce-scatter / all-gather for prefill batches up to
+    ``max_num_batched_tokens``; larger tensors use NCCL."""
     from . import comm
     from .state import get_tp
 
@@ -137,7 +216,7 @@ def maybe_enable_fused_comm(config, runner) -> Optional[FusedComm]:
     if tp.size == 1 or runner.device.type != "cuda":
         return None
     fc = FusedComm(tp, config.spec.hidden_size, runner.device, max_tokens=min(64, config.max_graph_batch or 64),
-                   timeout_s=config.comm_timeout_s)
+                   timeout_s=config.comm_timeout_s, sp_max_tokens=config.max_num_batched_tokens)
     comm.set_fused_comm(fc)
     runner.fused_comm = fc
     return fc

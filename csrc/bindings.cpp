@@ -2,12 +2,21 @@
 #include <torch/extension.h>
 
 namespace braid {
-void gemm(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
-          c10::optional<torch::Tensor> residual, int64_t epi, double rs_eps);
+int64_t gemm(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
+             c10::optional<torch::Tensor> residual, int64_t epi, double rs_eps, c10::optional<torch::Tensor> rs_vec,
+             c10::optional<torch::Tensor> sp);
 void gemm_qkv(torch::Tensor q_out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
               double rs_eps, torch::Tensor positions, torch::Tensor slots, torch::Tensor kv,
               c10::optional<torch::Tensor> q_norm, c10::optional<torch::Tensor> k_norm, double head_eps,
-              torch::Tensor cos, torch::Tensor sin, int64_t Hq, int64_t Hkv, int64_t D, bool use_rope);
+              torch::Tensor cos, torch::Tensor sin, int64_t Hq, int64_t Hkv, int64_t D, bool use_rope,
+              c10::optional<torch::Tensor> rs_vec, c10::optional<torch::Tensor> sp);
+void row_rstd(torch::Tensor x, double eps, torch::Tensor out);
+int64_t sp_reduce_allgather(torch::Tensor peers, int64_t recv_off, int64_t rs_flags_off, int64_t ag_flags_off,
+                            int64_t g_off, int64_t rstd_off, int64_t rank, int64_t tp, int64_t rpr, int64_t T,
+                            int64_t H, int64_t rs_expected, double eps, torch::Tensor status, double timeout_s);
+void sp_wait(int64_t local_ptr, int64_t ag_flags_off, int64_t tp, int64_t rank, int64_t expected,
+             torch::Tensor status, double timeout_s);
+torch::Tensor comm_tensor(int64_t ptr, int64_t offset, std::vector<int64_t> shape, int64_t dtype, int64_t device);
 int64_t gemm_check_error(int64_t device);
 void gemm_set_trace(torch::Tensor buf);
 int64_t gemm_push(torch::Tensor x, torch::Tensor w, torch::Tensor peers, int64_t flags_off, int64_t rank, int64_t tp,
@@ -43,8 +52,19 @@ void sample(torch::Tensor out, torch::Tensor logits, torch::Tensor temperature, 
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "braidinfer_b200 native sm_100a kernels";
-  m.def("gemm", &braid::gemm, "tcgen05 GEMM out = x @ w^T (+bias)(+residual); epi 1 = SwiGLU");
-  m.def("gemm_qkv", &braid::gemm_qkv, "tcgen05 QKV GEMM with fused q/k-norm, RoPE(k) and paged KV append");
+  m.def("gemm", &braid::gemm, "tcgen05 GEMM out = x @ w^T (+bias)(+residual); epi 1 = SwiGLU, 4 = reduce-scatter",
+        py::arg("out"), py::arg("x"), py::arg("w"), py::arg("bias"), py::arg("residual"), py::arg("epi"),
+        py::arg("rs_eps"), py::arg("rs_vec") = py::none(), py::arg("sp") = py::none());
+  m.def("gemm_qkv", &braid::gemm_qkv, "tcgen05 QKV GEMM with fused q/k-norm, RoPE(k) and paged KV append",
+        py::arg("q_out"), py::arg("x"), py::arg("w"), py::arg("bias"), py::arg("rs_eps"), py::arg("positions"),
+        py::arg("slots"), py::arg("kv"), py::arg("q_norm"), py::arg("k_norm"), py::arg("head_eps"), py::arg("cos"),
+        py::arg("sin"), py::arg("Hq"), py::arg("Hkv"), py::arg("D"), py::arg("use_rope"),
+        py::arg("rs_vec") = py::none(), py::arg("sp") = py::none());
+  m.def("row_rstd", &braid::row_rstd, "out[t] = 1/rms(x[t]) in fp32");
+  m.def("sp_reduce_allgather", &braid::sp_reduce_allgather,
+        "sequence-parallel reduce of pushed partial rows + all-gather of the new rows and their 1/rms");
+  m.def("sp_wait", &braid::sp_wait, "bounded wait for every owner's all-gather");
+  m.def("comm_tensor", &braid::comm_tensor, "tensor view of comm-buffer memory");
   m.def("gemm_push", &braid::gemm_push, "row-parallel GEMM whose epilogue pushes bf16 tiles to TP peers");
   m.def("comm_alloc", &braid::comm_alloc, "cudaMalloc a comm buffer; returns (ptr, ipc handle)");
   m.def("comm_open", &braid::comm_open, "map a peer's comm buffer from its IPC handle");

@@ -27,14 +27,9 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include "common.cuh"
+#include "launch.cuh"
 
 namespace braid {
-
-BRAID_DEVICE uint64_t ld_acquire_sys_u64(const uint64_t* p) {
-  uint64_t v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
 
 // Layout of one rank's communication buffer (offsets in bytes):
 //   [0, data_bytes)                recv[2][tp][maxT][H] bf16
@@ -133,6 +128,106 @@ __global__ void tp_reduce_add_kernel(__nv_bfloat16* __restrict__ residual, int T
   }
 }
 
+// -------------------------------------------- sequence parallel (prefill)
+// Reduce + all-gather of row-parallel GEMM partials for prefill-sized batches.
+// This rank owns token rows [rank*rpr, rank*rpr + rpr).  The GEMM epilogue
+// (epi 4) pushed every source's bf16 partial rows of this block into
+// recv[src]; one warp per owned row waits (bounded) for every source's tile
+// count, sums the tp partials in fp32, adds the residual row held in the
+// gathered buffer G, computes the row's 1/rms, and stores the new row and its
+// 1/rms into G / rstd of EVERY rank (peer stores over NVLink), then bumps each
+// rank's all-gather counter for this owner once per CTA.  The next GEMM waits
+// on that counter tile by tile (sp_wait_rows), so the gather overlaps its math.
+__global__ void __launch_bounds__(256) sp_reduce_allgather_kernel(
+    const uint64_t* __restrict__ peers, int64_t recv_off, int64_t rs_flags_off, int64_t ag_flags_off, int64_t g_off,
+    int64_t rstd_off, int rank, int tp, int rpr, int T, int H, uint64_t rs_expected, float eps, int* status,
+    uint64_t timeout_ns) {
+  __shared__ int s_fail;
+  pdl_wait();
+  const char* local = reinterpret_cast<const char*>(peers[rank]);
+  if (threadIdx.x == 0) s_fail = 0;
+  __syncthreads();
+  if (threadIdx.x < tp) {
+    const uint64_t* f = reinterpret_cast<const uint64_t*>(local + rs_flags_off) + threadIdx.x;
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire_sys_u64(f) < rs_expected) {
+      if (globaltimer_ns() - t0 > timeout_ns) {
+        if (atomicCAS(status, 0, 3) == 0) {
+          status[1] = rank;
+          status[2] = threadIdx.x;
+          status[3] = (int)rs_expected;
+        }
+        s_fail = 1;
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  __syncthreads();
+  if (s_fail) return;  // no all-gather signal: the consumers time out and report
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int lr = blockIdx.x * 8 + warp;
+  const int row = rank * rpr + lr;
+  if (lr < rpr && row < T) {
+    const __nv_bfloat16* recv = reinterpret_cast<const __nv_bfloat16*>(local + recv_off);
+    const __nv_bfloat16* g_row = reinterpret_cast<const __nv_bfloat16*>(local + g_off) + (size_t)row * H;
+    float ss = 0.f;
+    for (int c = lane * 8; c < H; c += 256) {
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int src = 0; src < tp; ++src) {
+        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(recv + ((size_t)src * rpr + lr) * H + c));
+        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] += bf2f(e[j]);
+      }
+      uint4 rv = *reinterpret_cast<const uint4*>(g_row + c);
+      __nv_bfloat16* re = reinterpret_cast<__nv_bfloat16*>(&rv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        re[j] = f2bf(bf2f(re[j]) + rbf(acc[j]));
+        const float y = bf2f(re[j]);
+        ss += y * y;
+      }
+      for (int p = 0; p < tp; ++p)
+        *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<char*>(peers[p]) + g_off) +
+                                  (size_t)row * H + c) = rv;
+    }
+    ss = warp_sum(ss);
+    if (lane < tp)
+      reinterpret_cast<float*>(reinterpret_cast<char*>(peers[lane]) + rstd_off)[row] = rsqrtf(ss / H + eps);
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    for (int p = 0; p < tp; ++p)
+      atomicAdd(reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(peers[p]) + ag_flags_off) + rank, 1ull);
+  }
+}
+
+// Bounded wait until every owner's all-gather count reaches `expected`; later
+// kernels on the stream may then read all of G with plain loads.
+__global__ void sp_wait_kernel(const char* __restrict__ local, int64_t ag_flags_off, int tp, int rank,
+                               uint64_t expected, int* status, uint64_t timeout_ns) {
+  pdl_wait();
+  if (threadIdx.x < tp) {
+    const uint64_t* f = reinterpret_cast<const uint64_t*>(local + ag_flags_off) + threadIdx.x;
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire_sys_u64(f) < expected) {
+      if (globaltimer_ns() - t0 > timeout_ns) {
+        if (atomicCAS(status, 0, 2) == 0) {
+          status[1] = rank;
+          status[2] = threadIdx.x;
+          status[3] = (int)expected;
+        }
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  __threadfence();
+}
+
 // ------------------------------------------------------------------ host
 // cudaMalloc'd communication buffer + its IPC handle (64 bytes, CPU uint8 tensor).
 std::vector<torch::Tensor> comm_alloc(int64_t nbytes, int64_t device) {
@@ -196,6 +291,35 @@ void tp_reduce_add(torch::Tensor out, torch::Tensor residual, bool add_residual,
       status.data_ptr<int>(), (uint64_t)(timeout_s * 1e9), add_residual ? 1 : 0,
       reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Returns the all-gather arrivals each rank receives from this owner per call (CTAs).
+int64_t sp_reduce_allgather(torch::Tensor peers, int64_t recv_off, int64_t rs_flags_off, int64_t ag_flags_off,
+                            int64_t g_off, int64_t rstd_off, int64_t rank, int64_t tp, int64_t rpr, int64_t T,
+                            int64_t H, int64_t rs_expected, double eps, torch::Tensor status, double timeout_s) {
+  TORCH_CHECK(peers.is_cuda() && peers.scalar_type() == at::kLong && peers.numel() == tp);
+  TORCH_CHECK(H % 8 == 0, "sp_reduce_allgather: hidden size must be a multiple of 8");
+  const at::cuda::CUDAGuard g(peers.device());
+  const int blocks = std::max<int64_t>(1, (rpr + 7) / 8);
+  launch_pdl(sp_reduce_allgather_kernel, dim3(blocks), dim3(256), 0, at::cuda::getCurrentCUDAStream(),
+             reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>()), recv_off, rs_flags_off, ag_flags_off,
+             g_off, rstd_off, (int)rank, (int)tp, (int)rpr, (int)T, (int)H, (uint64_t)rs_expected, (float)eps,
+             status.data_ptr<int>(), (uint64_t)(timeout_s * 1e9));
+  return blocks;
+}
+
+void sp_wait(int64_t local_ptr, int64_t ag_flags_off, int64_t tp, int64_t rank, int64_t expected,
+             torch::Tensor status, double timeout_s) {
+  const at::cuda::CUDAGuard g(status.device());
+  launch_pdl(sp_wait_kernel, dim3(1), dim3(32), 0, at::cuda::getCurrentCUDAStream(),
+             reinterpret_cast<const char*>(local_ptr), ag_flags_off, (int)tp, (int)rank, (uint64_t)expected,
+             status.data_ptr<int>(), (uint64_t)(timeout_s * 1e9));
+}
+
+// A tensor view of comm-buffer memory (no ownership; the buffer outlives it).
+torch::Tensor comm_tensor(int64_t ptr, int64_t offset, std::vector<int64_t> shape, int64_t dtype, int64_t device) {
+  auto opts = torch::TensorOptions().dtype(dtype == 0 ? at::kBFloat16 : at::kFloat).device(torch::kCUDA, device);
+  return torch::from_blob(reinterpret_cast<char*>(ptr) + offset, shape, opts);
 }
 
 }  // namespace braid

@@ -60,6 +60,17 @@ BRAID_DEVICE uint64_t globaltimer_ns() {
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
+
+// Acquire load at system scope (flags written by peer GPUs over NVLink).
+BRAID_DEVICE uint64_t ld_acquire_sys_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Orders this thread's earlier generic-proxy accesses (and what they acquired)
+// before its later async-proxy (TMA) accesses of global memory.
+BRAID_DEVICE void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 // Bounded wait on an mbarrier phase: gives up after `timeout_ns` of wall time
 // (checked every 256 polls).  Returns false on timeout so the caller can
 // record an error and unwind instead of hanging the GPU.

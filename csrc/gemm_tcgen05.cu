@@ -35,64 +35,11 @@
 #include <vector>
 
 #include "common.cuh"
+#include "gemm_types.cuh"
 #include "launch.cuh"
 
 namespace braid {
 
-// Fused QKV epilogue (epi == 2): per-head q/k RMSNorm, RoPE on k, q written
-// unrotated to q_out, k/v appended to the paged KV cache at slots[token].
-struct QkvEpi {
-  __nv_bfloat16* q_out;  // [T, Hq, D]
-  __nv_bfloat16* kv;     // layer cache [P, 2, Hkv, PS, D]
-  const int* slots;
-  const int* positions;
-  const __nv_bfloat16* q_norm;
-  const __nv_bfloat16* k_norm;
-  const float* cos;
-  const float* sin;
-  int Hq, Hkv, D, PS, use_rope;
-  float eps;
-};
-
-// Push epilogue (epi == 3, swapped mode): the bf16 result tile is written to
-// every tensor-parallel peer's receive area (slot epoch & 1, source row rank)
-// instead of local memory, then each peer's arrival counter for this rank is
-// bumped; tp_reduce_add in comm.cu completes the all-reduce.
-struct PushEpi {
-  const uint64_t* peers;       // [tp] base addresses of the peers' comm buffers
-  int64_t flags_off;           // byte offset of the arrival counters in a comm buffer
-  const uint64_t* epoch_state; // local epoch (completed all-reduce calls)
-  int rank, tp, maxT;
-};
-
-struct GemmArgs {
-  int M, N, K;        // A rows, B rows, reduction length
-  int swap;           // 1: A is the weight, output written transposed
-  int epi;            // 0 plain, 1 swiglu, 2 qkv, 3 push
-  __nv_bfloat16* out;
-  int ldo;
-  const __nv_bfloat16* bias;      // indexed by feature
-  const __nv_bfloat16* residual;  // same layout as out
-  int ldr;
-  // Fused input RMSNorm: the norm weight is folded into the weight matrix and
-  // each token's 1/rms(x) is applied here (x = the activation operand).
-  const __nv_bfloat16* rs_x;
-  int rs_ld;
-  float rs_eps;
-  int splits;
-  int kb_per_split;
-  int cluster;        // 1: the split-K CTAs of a tile form one cluster and reduce through DSMEM
-  float* ws;          // split-K partials (global path)
-  int* counters;      // one per output tile, kept at zero between launches
-  int* err;           // error flag (bounded-wait timeout)
-  QkvEpi qkv;
-  PushEpi push;
-  unsigned long long* trace;  // optional per-CTA phase timestamps (profiling)
-};
-
-constexpr int BM = 128;
-constexpr int BK = 64;
-constexpr int XCH_LD = 17;  // exchange tile: 128 rows x 16 columns (+1 pad) fp32
 
 template <int BN, int STAGES>
 struct GemmSmem {
@@ -218,6 +165,8 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
         tma_load_2d(ringA + i * S::A_BYTES, &tmA, &full[i], (kb0 + i) * BK, m0);
       }
       pdl_wait();
+      // sequence-parallel prefill: the A rows must have been gathered from their owners
+      if (!args.swap && !sp_wait_rows(args.sp, m0, min(m0 + BM, args.M))) atomicExch(args.err, 4);
       for (int i = 0; i < pre; ++i) tma_load_2d(ringB + i * S::B_BYTES, &tmB, &full[i], (kb0 + i) * BK, n0);
       for (int i = pre; i < nkb; ++i) {
         const int s = i % STAGES;
@@ -294,6 +243,10 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
     if (tr != nullptr && et == 0) tr[3] = globaltimer_ns();
     tc_fence_after();
     has_acc = ready && nkb > 0;
+    if (args.rs_vec != nullptr && !args.swap && m0 + r < args.M) {
+      sp_wait_rows(args.sp, m0 + r, m0 + r + 1);
+      rs_row = args.rs_vec[m0 + r];
+    }
     if (args.cluster) {
       // Cluster split-K: stage this slice's fp32 partial in the (now idle) A ring.
       float* part = reinterpret_cast<float*>(ringA) + (size_t)r * BN;
@@ -393,7 +346,7 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
 #pragma unroll
           for (int j = 0; j < 16; ++j) v[j] = 0.f;
         }
-        if (args.rs_x != nullptr) {
+        if (args.rs_x != nullptr || args.rs_vec != nullptr) {
 #pragma unroll
           for (int j = 0; j < 16; ++j) v[j] *= args.swap ? rstd_s[c0 + j] : rs_row;
         }
@@ -409,47 +362,13 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
         }
       };
 
-      if (args.epi == 0) {
+      if (!args.swap) {
+        store_tile_normal<BN>(args, m0, n0, r, load_cols);
+      } else if (args.epi == 0) {
         for (int c0 = 0; c0 < BN; c0 += 16) {
           float v[16];
           load_cols(c0, v);
-          if (!args.swap) {
-            const int m = m0 + r;
-            if (m < args.M) {
-              __nv_bfloat16* o = args.out + (size_t)m * args.ldo + n0 + c0;
-              const __nv_bfloat16* res = args.residual ? args.residual + (size_t)m * args.ldr + n0 + c0 : nullptr;
-              const bool vec = n0 + c0 + 16 <= args.N && ((reinterpret_cast<uintptr_t>(o) |
-                               reinterpret_cast<uintptr_t>(res)) & 15) == 0;
-              if (vec) {
-                // 16 outputs = two 16-byte stores (the row is this thread's)
-                uint4 rv[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
-                if (res) {
-                  rv[0] = *reinterpret_cast<const uint4*>(res);
-                  rv[1] = *reinterpret_cast<const uint4*>(res + 8);
-                }
-                const __nv_bfloat16* re = reinterpret_cast<const __nv_bfloat16*>(rv);
-                uint4 ov[2];
-                __nv_bfloat16* oe = reinterpret_cast<__nv_bfloat16*>(ov);
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                  float y = rbf(v[j]);
-                  if (res) y += bf2f(re[j]);
-                  oe[j] = f2bf(y);
-                }
-                *reinterpret_cast<uint4*>(o) = ov[0];
-                *reinterpret_cast<uint4*>(o + 8) = ov[1];
-              } else {
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                  if (n0 + c0 + j < args.N) {
-                    float y = rbf(v[j]);
-                    if (res) y += bf2f(res[j]);
-                    o[j] = f2bf(y);
-                  }
-                }
-              }
-            }
-          } else {
+          {
             const int m = m0 + r;  // feature
             if (m < args.M) {
 #pragma unroll
@@ -492,35 +411,6 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
             atomicAdd(reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(ps.peers[p]) + ps.flags_off) +
                           ps.rank, 1ull);
         }
-      } else if (args.epi == 1 && !args.swap) {
-        // Normal SwiGLU: per 128-column block, gate = cols [0,64), up = [64,128).
-        const int m = m0 + r;
-        for (int blk = 0; blk < BN / 128; ++blk) {
-          for (int c0 = 0; c0 < 64; c0 += 16) {
-            float g[16], u[16];
-            load_cols(blk * 128 + c0, g);
-            load_cols(blk * 128 + 64 + c0, u);
-            if (m < args.M) {
-              const int f0 = (n0 + blk * 128) / 2 + c0;
-              __nv_bfloat16* o = args.out + (size_t)m * args.ldo + f0;
-              uint4 ov[2];
-              __nv_bfloat16* oe = reinterpret_cast<__nv_bfloat16*>(ov);
-#pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                const float gg = rbf(g[j]), uu = rbf(u[j]);
-                const float sg = rbf(gg / (1.f + __expf(-gg)));
-                oe[j] = f2bf(sg * uu);
-              }
-              if (2 * (f0 + 16) <= args.N && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
-                *reinterpret_cast<uint4*>(o) = ov[0];
-                *reinterpret_cast<uint4*>(o + 8) = ov[1];
-              } else {
-                for (int j = 0; j < 16; ++j)
-                  if (2 * (f0 + j) < args.N) o[j] = oe[j];
-              }
-            }
-          }
-        }
       } else if (args.epi == 1) {
         // Swapped SwiGLU: tile rows [0,64) gate, [64,128) up of the same 64 features.
         for (int c0 = 0; c0 < BN; c0 += 16) {
@@ -547,7 +437,7 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
           }
           named_bar_sync(1, 128);
         }
-      } else if (args.swap) {
+      } else {
         // Swapped QKV: rows = 128 features (one D=128 head or two D=64 heads),
         // columns = tokens.  Stage 16 tokens at a time, then one warp per token.
         const int D = args.qkv.D;
@@ -577,72 +467,6 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
             }
           }
           named_bar_sync(1, 128);
-        }
-      } else {
-        // Normal QKV: this thread owns token row m and whole heads of the tile.
-        const int D = args.qkv.D;
-        const int m = m0 + r;
-        const QkvEpi& q = args.qkv;
-        for (int hl = 0; hl < BN / D; ++hl) {
-          const int col0 = hl * D;
-          if (n0 + col0 >= args.N) break;
-          const int head = (n0 + col0) / D;
-          const bool is_q = head < q.Hq, is_k = !is_q && head < q.Hq + q.Hkv;
-          const __nv_bfloat16* nw = is_q ? q.q_norm : (is_k ? q.k_norm : nullptr);
-          float hr = 1.f;
-          if (nw != nullptr) {
-            float ss = 0.f;
-            for (int c = 0; c < D; c += 16) {
-              float v[16];
-              load_cols(col0 + c, v);
-#pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                const float y = rbf(v[j]);
-                ss += y * y;
-              }
-            }
-            hr = rsqrtf(ss / D + q.eps);
-          }
-          if (m >= args.M) continue;
-          __nv_bfloat16* dst;
-          if (is_q) {
-            dst = q.q_out + ((size_t)m * q.Hq + head) * D;
-          } else {
-            const int slot = q.slots[m];
-            const int kh = is_k ? head - q.Hq : head - q.Hq - q.Hkv;
-            dst = q.kv + ((((size_t)(slot / q.PS)) * 2 + (is_k ? 0 : 1)) * q.Hkv + kh) * q.PS * (size_t)D +
-                  (size_t)(slot % q.PS) * D;
-          }
-          const int pos = q.positions[m];
-          for (int c = 0; c < D / 2; c += 16) {
-            float a[16], b[16];
-            load_cols(col0 + c, a);
-            load_cols(col0 + D / 2 + c, b);
-            uint4 w1[2], w2[2];
-            __nv_bfloat16* e1 = reinterpret_cast<__nv_bfloat16*>(w1);
-            __nv_bfloat16* e2 = reinterpret_cast<__nv_bfloat16*>(w2);
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              float x1 = rbf(a[j]), x2 = rbf(b[j]);
-              if (nw != nullptr) {
-                x1 = rbf(rbf(x1 * hr) * bf2f(nw[c + j]));
-                x2 = rbf(rbf(x2 * hr) * bf2f(nw[D / 2 + c + j]));
-              }
-              if (is_k && q.use_rope) {
-                const float cs = q.cos[(size_t)pos * (D / 2) + c + j], sn = q.sin[(size_t)pos * (D / 2) + c + j];
-                const float y1 = x1 * cs - x2 * sn, y2 = x2 * cs + x1 * sn;
-                x1 = y1;
-                x2 = y2;
-              }
-              e1[j] = f2bf(x1);
-              e2[j] = f2bf(x2);
-            }
-            // head rows are 16-byte aligned (D and c are multiples of 8)
-            *reinterpret_cast<uint4*>(dst + c) = w1[0];
-            *reinterpret_cast<uint4*>(dst + c + 8) = w1[1];
-            *reinterpret_cast<uint4*>(dst + D / 2 + c) = w2[0];
-            *reinterpret_cast<uint4*>(dst + D / 2 + c + 8) = w2[1];
-          }
         }
       }
     }
@@ -764,7 +588,7 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs&
                      a);
 }
 
-static int num_sms() {
+int gemm_num_sms() {
   static int n = 0;
   if (!n) {
     int dev;
@@ -786,7 +610,31 @@ static inline const __nv_bfloat16* opt_bf(const c10::optional<torch::Tensor>& t)
 }
 
 // Common driver: picks operand roles, tile width, split-K and launches.
-static void run_gemm(GemmArgs& a, const torch::Tensor& x, const torch::Tensor& w, bool fused_rms) {
+void launch_row_rstd(const __nv_bfloat16* x, int ld, int T, int K, float eps, float* out, cudaStream_t st);
+
+// Sequence-parallel parameters from a CPU int64 tensor: [peers (device address of
+// int64[tp]), recv_off, rs_flags_off, ag_flags_off, ag_expected, status (device
+// address), timeout_ns, rank, tp, rows_per_rank, H].
+static void fill_sp(GemmArgs& a, const c10::optional<torch::Tensor>& sp) {
+  if (!sp.has_value() || !sp->defined()) return;
+  TORCH_CHECK(!sp->is_cuda() && sp->scalar_type() == at::kLong && sp->numel() >= 11, "gemm: bad sp params");
+  const int64_t* v = sp->data_ptr<int64_t>();
+  SpArgs& p = a.sp;
+  p.peers = reinterpret_cast<const uint64_t*>(v[0]);
+  p.recv_off = v[1];
+  p.rs_flags_off = v[2];
+  p.ag_flags_off = v[3];
+  p.ag_expected = (uint64_t)v[4];
+  p.status = reinterpret_cast<int*>(v[5]);
+  p.timeout_ns = (uint64_t)v[6];
+  p.rank = (int)v[7];
+  p.tp = (int)v[8];
+  p.rows_per_rank = (int)v[9];
+  p.H = (int)v[10];
+  TORCH_CHECK(p.rows_per_rank > 0 && p.tp > 0, "gemm: bad sp layout");
+}
+
+static int64_t run_gemm(GemmArgs& a, const torch::Tensor& x, const torch::Tensor& w, bool fused_rms) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda(), "gemm: CUDA tensors required");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "gemm: bf16 only");
   TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1), "gemm: shape mismatch");
@@ -796,14 +644,14 @@ static void run_gemm(GemmArgs& a, const torch::Tensor& x, const torch::Tensor& w
   TORCH_CHECK((reinterpret_cast<uintptr_t>(x.data_ptr()) & 15) == 0 &&
               (reinterpret_cast<uintptr_t>(w.data_ptr()) & 15) == 0, "gemm: 16-byte aligned operands required");
   if (a.epi == 1) TORCH_CHECK(F % 128 == 0, "gemm: swiglu weight rows must be a multiple of 128");
-  if (T == 0) return;
+  if (T == 0) return 0;
   const at::cuda::CUDAGuard guard(x.device());
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   a.K = K;
   a.rs_x = fused_rms ? reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()) : nullptr;
   a.rs_ld = x.stride(0);
   const int kb_total = (K + BK - 1) / BK;
-  const bool swap = T <= 64;
+  const bool swap = T <= 64 && a.epi != 4 && a.rs_vec == nullptr && a.sp.peers == nullptr;
   a.swap = swap;
   int BN, m_tiles, n_tiles;
   if (swap) {
@@ -820,10 +668,40 @@ static void run_gemm(GemmArgs& a, const torch::Tensor& x, const torch::Tensor& w
     n_tiles = (F + BN - 1) / BN;
   }
   const int tiles = m_tiles * n_tiles;
+  // reduce-scatter epilogue: partial tiles this rank (as row owner) receives from every source
+  int64_t arrivals = 0;
+  if (a.epi == 4) {
+    TORCH_CHECK(a.sp.peers != nullptr && a.sp.H == F, "gemm: epi 4 needs sequence-parallel params");
+    const int r0 = a.sp.rank * a.sp.rows_per_rank, r1 = std::min(T, r0 + a.sp.rows_per_rank);
+    if (r1 > r0) arrivals = (int64_t)n_tiles * ((r1 - 1) / BM - r0 / BM + 1);
+  }
+  static const bool persist_on = [] {  // tuning knob: BRAID_GEMM_PERSISTENT=0 keeps one tile per CTA
+    const char* e = getenv("BRAID_GEMM_PERSISTENT");
+    return !(e && e[0] == '0');
+  }();
+  if (!swap && persist_on && tiles >= gemm_num_sms()) {
+    torch::Tensor rstd;
+    if (fused_rms && a.rs_vec == nullptr) {
+      rstd = torch::empty({T}, x.options().dtype(at::kFloat));
+      launch_row_rstd(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), T, K, a.rs_eps,
+                      rstd.data_ptr<float>(), st);
+      a.rs_vec = rstd.data_ptr<float>();
+    }
+    a.rs_x = nullptr;
+    a.splits = 1;
+    a.kb_per_split = kb_total;
+    a.cluster = 0;
+    a.err = scratch_for(x.get_device(), 0, 0).err;
+    CUtensorMap ta = make_tmap(x.data_ptr(), T, K, x.stride(0), BM);
+    CUtensorMap tb = make_tmap(w.data_ptr(), F, K, w.stride(0), BN);
+    launch_gemm_persistent(ta, tb, a, BN, st);
+    return arrivals;
+  }
+  if (a.rs_vec != nullptr) a.rs_x = nullptr;
   // Split-K so that one wave of resident CTAs (2 per SM for decode tiles)
   // covers the machine; decode shapes have few output tiles.
   int splits = 1;
-  const int slots = num_sms() * (swap ? 2 : 1);
+  const int slots = gemm_num_sms() * (swap ? 2 : 1);
   if (tiles < slots) splits = std::max(1, std::min({slots / tiles, kb_total / 2, 16}));
   static const int forced = [] {  // tuning knob: BRAID_GEMM_SPLITS=n forces the split-K factor
     const char* e = getenv("BRAID_GEMM_SPLITS");
@@ -862,12 +740,18 @@ static void run_gemm(GemmArgs& a, const torch::Tensor& x, const torch::Tensor& w
     case 128: launch<128, 6>(ta, tb, a, grid, st); break;
     default: launch<256, 4>(ta, tb, a, grid, st); break;
   }
+  return arrivals;
 }
 
 // out = rms?(x) @ w^T (+bias) (+residual); epi: 0 plain, 1 swiglu (w block-interleaved).
 // rs_eps >= 0 enables the fused input RMSNorm (w must carry the folded norm weight).
-void gemm(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
-          c10::optional<torch::Tensor> residual, int64_t epi, double rs_eps) {
+// rs_vec (float [T]) supplies precomputed 1/rms per token instead; sp carries the
+// sequence-parallel parameters (epi 4 = reduce-scatter push, and the all-gather
+// wait before A rows are read).  Returns, for epi 4, the partial tiles this rank
+// receives from each source.
+int64_t gemm(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
+             c10::optional<torch::Tensor> residual, int64_t epi, double rs_eps, c10::optional<torch::Tensor> rs_vec,
+             c10::optional<torch::Tensor> sp) {
   TORCH_CHECK(out.is_cuda() && out.stride(1) == 1, "gemm: out must be row-contiguous");
   GemmArgs a{};
   a.epi = (int)epi;
@@ -877,7 +761,12 @@ void gemm(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<tor
   a.residual = opt_bf(residual);
   a.ldr = a.residual ? residual->stride(0) : 0;
   a.rs_eps = (float)rs_eps;
-  run_gemm(a, x, w, rs_eps >= 0);
+  if (rs_vec.has_value() && rs_vec->defined()) {
+    TORCH_CHECK(rs_vec->scalar_type() == at::kFloat && rs_vec->numel() >= x.size(0), "gemm: rs_vec");
+    a.rs_vec = rs_vec->data_ptr<float>();
+  }
+  fill_sp(a, sp);
+  return run_gemm(a, x, w, rs_eps >= 0 && a.rs_vec == nullptr);
 }
 
 // qkv = rms?(x) @ w^T (+bias), then per-head q/k RMSNorm, RoPE(k) and the
@@ -885,7 +774,8 @@ void gemm(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<tor
 void gemm_qkv(torch::Tensor q_out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
               double rs_eps, torch::Tensor positions, torch::Tensor slots, torch::Tensor kv,
               c10::optional<torch::Tensor> q_norm, c10::optional<torch::Tensor> k_norm, double head_eps,
-              torch::Tensor cos, torch::Tensor sin, int64_t Hq, int64_t Hkv, int64_t D, bool use_rope) {
+              torch::Tensor cos, torch::Tensor sin, int64_t Hq, int64_t Hkv, int64_t D, bool use_rope,
+              c10::optional<torch::Tensor> rs_vec, c10::optional<torch::Tensor> sp) {
   TORCH_CHECK(D == 64 || D == 128, "gemm_qkv: head_dim must be 64 or 128");
   TORCH_CHECK(w.size(0) == (Hq + 2 * Hkv) * D, "gemm_qkv: weight rows != (Hq + 2 Hkv) * D");
   TORCH_CHECK(kv.is_contiguous() && kv.size(2) == Hkv && kv.size(4) == D, "gemm_qkv: cache layout");
@@ -909,7 +799,12 @@ void gemm_qkv(torch::Tensor q_out, torch::Tensor x, torch::Tensor w, c10::option
   q.PS = kv.size(3);
   q.use_rope = use_rope ? 1 : 0;
   q.eps = (float)head_eps;
-  run_gemm(a, x, w, rs_eps >= 0);
+  if (rs_vec.has_value() && rs_vec->defined()) {
+    TORCH_CHECK(rs_vec->scalar_type() == at::kFloat && rs_vec->numel() >= x.size(0), "gemm_qkv: rs_vec");
+    a.rs_vec = rs_vec->data_ptr<float>();
+  }
+  fill_sp(a, sp);
+  run_gemm(a, x, w, rs_eps >= 0 && a.rs_vec == nullptr);
 }
 
 int64_t gemm_check_error(int64_t device) {
@@ -1047,7 +942,7 @@ extern "C" int braid_gemm_noalloc(void* out, const void* x, const void* w, const
   const int tiles = m_tiles;
   const int kb_total = (K + BK - 1) / BK;
   int splits = 1;
-  const int slots = num_sms() * 2;
+  const int slots = gemm_num_sms() * 2;
   if (tiles < slots) splits = std::max(1, std::min({slots / tiles, kb_total / 2, 32}));
   // never more scratch than the fixed array holds
   while (splits > 1 && ((size_t)tiles * splits * BM * BN * 4 > BRAID_NOALLOC_PARTIAL_BYTES || tiles > BRAID_NOALLOC_MAX_TILES))

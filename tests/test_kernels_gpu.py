@@ -105,6 +105,65 @@ def test_gemm_qkv_epilogue(T, D, Hq, Hkv, qk_norm, bias):
     _check_err()
 
 
+@pytest.mark.parametrize("M,N,K,mode", [(1000, 6144, 1024, "bias_res"), (700, 8192, 1024, "swiglu"),
+                                        (777, 8192, 2048, "rms"), (1000, 2560, 512, "plain"),
+                                        (4100, 4096, 1024, "bias_res")])
+def test_gemm_persistent(M, N, K, mode):
+    """Shapes with >= one tile per SM run the persistent kernel (double-buffered
+    TMEM accumulators); compare with the fp32 reference of the same op."""
+    from braidinfer_b200 import ops
+    from braidinfer_b200.ops.linear import swiglu_ref_from_interleaved
+    g = torch.Generator(device=DEV).manual_seed(M + N + K)
+    x = (torch.randn(M, K, device=DEV, generator=g) * (3 if mode == "rms" else 1)).bfloat16()
+    w = (torch.randn(N, K, device=DEV, generator=g) * 0.05).bfloat16()
+    tol = dict(atol=3e-2 * math.sqrt(K / 256), rtol=3e-2)
+    if mode == "swiglu":
+        out = ops.linear_swiglu(x, w)
+        ref = swiglu_ref_from_interleaved(x.float() @ w.float().t(), torch.bfloat16)
+        torch.testing.assert_close(out.float(), ref.float(), **tol)
+    elif mode == "rms":
+        out = ops.linear(x, w, rms_eps=1e-5)
+        ref = (x.float() * torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + 1e-5)) @ w.float().t()
+        torch.testing.assert_close(out.float(), ref, atol=5e-2, rtol=3e-2)
+        # precomputed 1/rms gives the same result
+        rs = ops.row_rstd(x, 1e-5)
+        out2 = torch.empty_like(out)
+        _ext().gemm(out2, x, w, None, None, 0, -1.0, rs, None)
+        torch.testing.assert_close(out2.float(), out.float(), atol=1e-2, rtol=1e-2)
+    elif mode == "bias_res":
+        b = torch.randn(N, device=DEV, generator=g).bfloat16()
+        r = torch.randn(M, N, device=DEV, generator=g).bfloat16()
+        out = ops.linear(x, w, b, residual=r.clone())
+        ref = (x.float() @ w.float().t() + b.float()).bfloat16().float() + r.float()
+        torch.testing.assert_close(out.float(), ref, atol=6e-2, rtol=2e-2)
+    else:
+        out = ops.linear(x, w)
+        torch.testing.assert_close(out.float(), x.float() @ w.float().t(), **tol)
+    torch.cuda.synchronize()
+    _check_err()
+
+
+def test_gemm_qkv_persistent():
+    """Prefill-sized fused QKV (persistent kernel) == linear + qkv_prepare."""
+    from braidinfer_b200 import ops
+    T, D, Hq, Hkv, H, PS, P = 1000, 128, 32, 8, 512, 16, 80
+    x = torch.randn(T, H, device=DEV).bfloat16()
+    w = (torch.randn((Hq + 2 * Hkv) * D, H, device=DEV) * 0.05).bfloat16()
+    pos = torch.arange(T, device=DEV, dtype=torch.int32)
+    slots = torch.randperm(P * PS, device=DEV)[:T].int()
+    cos, sin = ops.build_cos_sin(D, 10000.0, 1024, device=DEV)
+    qn = (torch.rand(D, device=DEV) * 2).bfloat16()
+    kn = (torch.rand(D, device=DEV) * 2).bfloat16()
+    kv1 = torch.zeros(P, 2, Hkv, PS, D, device=DEV, dtype=torch.bfloat16)
+    kv2 = kv1.clone()
+    q1 = ops.qkv_gemm(x, w, None, 1e-6, pos, slots, kv1, Hq, Hkv, D, cos, sin, qn, kn, 1e-6, True)
+    qkv = ops.linear(x, w, None, rms_eps=1e-6)
+    q2 = ops.qkv_prepare(qkv, pos, slots, kv2, Hq, Hkv, D, cos, sin, qn, kn, 1e-6, True)
+    torch.testing.assert_close(q1.float(), q2.float(), atol=0.05, rtol=3e-2)
+    torch.testing.assert_close(kv1.float(), kv2.float(), atol=0.05, rtol=3e-2)
+    _check_err()
+
+
 def test_rmsnorm_and_add():
     from braidinfer_b200.ops.norm import rms_norm_ref
     for H in (256, 1024, 4096, 8192):

@@ -2,6 +2,9 @@
 off; our kernels use plain peer stores, never multimem).
 
 * the fused peer-memory all-reduce equals NCCL's;
+* the sequence-parallel prefill path (GEMM -> reduce-scatter epilogue, owner
+  reduce + all-gather of rows and 1/rms, all-gather -> fused-norm GEMM) equals
+  NCCL all-reduce + the single-GPU kernels;
 * a TP2 engine (fused and NCCL backends) matches TP1 logits;
 * a peer that never signals makes the bounded wait expire: both ranks get
   CommTimeoutError and the CUDA context stays usable.
@@ -66,6 +69,56 @@ def _w_allreduce(rank, world, port, q):
         torch.cuda.synchronize()
         fc.check()
         errs.append((out.float() - ref).abs().max().item())
+        q.put((rank, errs))
+        fc.close()
+    except Exception:
+        import traceback
+        q.put((rank, traceback.format_exc()))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def _w_seqpar(rank, world, port, q):
+    _env(rank, world, port)
+    import datetime
+    import torch.distributed as dist
+    try:
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+        from braidinfer_b200 import ops
+        from braidinfer_b200.parallel.state import init_tp
+        from braidinfer_b200.parallel.symm import FusedComm
+        tp = init_tp(world)
+        H, eps = 2048, 1e-5
+        fc = FusedComm(tp, H, torch.device("cuda", rank), max_tokens=16, timeout_s=5.0, sp_max_tokens=1280)
+        errs = []
+        # T=300: partial tiles span two owners, small-grid GEMMs; T=1200: persistent GEMMs
+        for it, (T, K) in enumerate([(300, 512), (1200, 1024), (300, 512), (97, 256)]):
+            gs = torch.Generator(device="cuda").manual_seed(1000 + it)  # same on every rank
+            gr = torch.Generator(device="cuda").manual_seed(2000 + 10 * it + rank)  # rank-local
+            res = torch.randn(T, H, device="cuda", generator=gs).bfloat16()
+            x = torch.randn(T, K, device="cuda", generator=gr).bfloat16()
+            w = (torch.randn(H, K, device="cuda", generator=gr) * 0.05).bfloat16()
+            part = (x.float() @ w.float().t()).bfloat16().float()
+            dist.all_reduce(part)
+            ref = (res.float() + part.bfloat16().float()).bfloat16()
+            G, rstd = fc.sp_begin(T)
+            G.copy_(res)
+            fc.sp_linear_reduce_scatter(x, w, G)
+            fc.sp_reduce_allgather(eps)
+            # all-gather -> fused-norm GEMM (SwiGLU, N = 8192 columns)
+            wgu = (torch.randn(8192, H, device="cuda", generator=gs) * 0.05).bfloat16()
+            y = ops.linear_swiglu(G, wgu, rms_eps=eps, rs_vec=rstd, sp=fc.sp_params())
+            fc.sp_wait()
+            torch.cuda.synchronize()
+            fc.check()
+            y_ref = ops.linear_swiglu(ref, wgu, rms_eps=eps)
+            rs_ref = torch.rsqrt(ref.float().pow(2).mean(-1) + eps)
+            # relative errors: G differs from the reference by bf16 rounding of the GEMM partials
+            errs.append(max((G.float() - ref.float()).abs().max().item() / ref.float().abs().max().item(),
+                            (rstd - rs_ref).abs().max().item() / rs_ref.abs().max().item(),
+                            (y.float() - y_ref.float()).abs().max().item() / y_ref.float().abs().max().item()))
         q.put((rank, errs))
         fc.close()
     except Exception:
@@ -147,6 +200,13 @@ def test_fused_all_reduce_matches_nccl():
     for r in _spawn(_w_allreduce, 2):
         assert isinstance(r[1], list), r[1]
         assert max(r[1]) < 0.05, r[1]
+
+
+@needs2
+def test_sequence_parallel_prefill_collectives():
+    for r in _spawn(_w_seqpar, 2):
+        assert isinstance(r[1], list), r[1]
+        assert max(r[1]) < 0.02, r[1]
 
 
 @needs2
