@@ -136,6 +136,7 @@ class Config:
     dtype: str = "auto"           # "auto" (bf16 on GPU, fp32 on CPU) | "bfloat16" | "float32"
     page_size: Optional[int] = None  # alias of kvcache_block_size
     max_graph_batch: int = 64     # largest decode batch captured in a CUDA graph
+    max_prefill_graph_tokens: int = 256  # single-sequence prefills up to this many tokens replay a graph
     comm_backend: str = "fused"   # "fused" (in-kernel peer stores) | "nccl" (baseline)
     comm_timeout_s: float = 5.0
     heartbeat_every: int = 0       # TP: check peer liveness every N engine steps (0 = off)

@@ -45,9 +45,12 @@ class Plan:
 
 
 def build_plan(items: List[FwdItem], page_size: int, pad_seqs: int = 0, scratch_page: int = 0,
-               seg_cap: Optional[int] = None, page_cap: Optional[int] = None) -> Plan:
+               seg_cap: Optional[int] = None, page_cap: Optional[int] = None, pad_tokens: int = -1) -> Plan:
     """Flatten ``items`` into the kernel metadata.  ``pad_seqs`` appends dummy
-    one-token sequences (CUDA-graph padding) that write to ``scratch_page``."""
+    one-token sequences (CUDA-graph padding) that write to ``scratch_page``;
+    ``pad_tokens >= 0`` appends ONE dummy sequence of that many tokens (padding
+    of a prefill graph's token count), also confined to ``scratch_page`` and
+    without a logits row."""
     ids, pos, slots = [], [], []
     qo, segi = [0], [0]
     spi, soff, slen, spos0, sdelta, pids = [0], [], [], [], [], []
@@ -103,6 +106,21 @@ def build_plan(items: List[FwdItem], page_size: int, pad_seqs: int = 0, scratch_
         lidx.append(len(ids) - 1)
         max_q = max(max_q, 1)
         max_kv = max(max_kv, 1)
+    if pad_tokens >= 0:
+        for j in range(pad_tokens):
+            ids.append(0)
+            pos.append(j)
+            slots.append(scratch_page * page_size + j % page_size)
+        qo.append(len(ids))
+        if pad_tokens > 0:
+            pids.append(scratch_page)
+            spi.append(len(pids))
+            soff.append(0)
+            slen.append(min(pad_tokens, page_size))
+            spos0.append(0)
+            sdelta.append(0)
+        segi.append(len(slen))
+        max_q = max(max_q, pad_tokens)
     S = len(slen)
     if seg_cap is not None:
         if S > seg_cap:
@@ -124,8 +142,8 @@ def build_plan(items: List[FwdItem], page_size: int, pad_seqs: int = 0, scratch_
     }
     arrays = {k: np.asarray(v, dtype=np.int32) for k, v in arrays.items()}
     sizes = {k: len(v) for k, v in arrays.items()}
-    return Plan(arrays, len(items) + pad_seqs, len(ids), max_q, max_kv,
-                decode=(max_q == 1 and len(ids) == len(items) + pad_seqs), sizes=sizes)
+    nseq = len(items) + pad_seqs + (1 if pad_tokens >= 0 else 0)
+    return Plan(arrays, nseq, len(ids), max_q, max_kv, decode=(max_q == 1 and len(ids) == nseq), sizes=sizes)
 
 
 def pack(plan: Plan) -> np.ndarray:

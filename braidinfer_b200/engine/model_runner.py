@@ -34,6 +34,8 @@ from .sequence import Sequence
 log = get_logger("runner")
 
 GRAPH_BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 192, 256)
+# token counts of single-sequence prefill graphs (a query or turn appended to cached chunks)
+PREFILL_BUCKETS = (16, 32, 64, 128, 256)
 
 
 def _num_sms(device) -> int:
@@ -85,6 +87,7 @@ class ModelRunner:
         self.capture_logits: Optional[list] = None  # debug/test hook (eager steps only)
         self.event_log: Optional[list] = None  # (start, end) CUDA events around each graph replay
         self.fused_comm = None  # set when the peer-memory TP runtime is enabled
+        self.prefill_graphs: Dict[int, _GraphSlot] = {}
         self.last_h2d_bytes = 0
 
     # ------------------------------------------------------------- KV pool
@@ -193,6 +196,11 @@ class ModelRunner:
             if out is not None:
                 self.timing["decode_tokens"] += len(seqs)
                 return out
+        if is_prefill and self.config.use_cuda_graphs and len(seqs) == 1 and self.capture_logits is None:
+            out = self._run_prefill_graph(seqs[0])
+            if out is not None:
+                self.timing["prefill_tokens"] += seqs[0].num_tokens - seqs[0].num_cached_tokens
+                return out
         with_tokens = [s for s in seqs if s.num_tokens > s.num_cached_tokens]
         rows = []
         if with_tokens:
@@ -245,18 +253,27 @@ class ModelRunner:
         pages_per_seq = -(-self.config.max_model_len // self.page_size) + max_segs
         return B * max_segs, B * pages_per_seq
 
-    def _capture(self, B: int) -> _GraphSlot:
+    def _capture(self, B: int, prefill_tokens: int = 0) -> _GraphSlot:
+        """Capture one engine step: a decode step of ``B`` sequences, or (with
+        ``prefill_tokens``) a prefill of one sequence padded to that many tokens."""
         g = _GraphSlot()
         g.seg_cap, g.page_cap = self._graph_caps(B)
         pm = self.page_manager
-        plan = build_plan([], self.page_size, pad_seqs=B, scratch_page=pm.scratch_page,
-                          seg_cap=g.seg_cap, page_cap=g.page_cap)
+        if prefill_tokens:
+            g.seg_cap, g.page_cap = g.seg_cap + 1, g.page_cap + 1  # + the padding sequence
+            dummy = FwdItem(tokens=[0], pos0=0, priv_index0=0, priv_pages=[pm.scratch_page], priv_pos0=0)
+            plan = build_plan([dummy], self.page_size, scratch_page=pm.scratch_page, seg_cap=g.seg_cap,
+                              page_cap=g.page_cap, pad_tokens=prefill_tokens - 1)
+        else:
+            plan = build_plan([], self.page_size, pad_seqs=B, scratch_page=pm.scratch_page,
+                              seg_cap=g.seg_cap, page_cap=g.page_cap)
         g.sizes = plan.sizes
         g.meta_buf = torch.from_numpy(pack(plan)).to(self.device)
         views = unpack(g.meta_buf, g.sizes)
-        g.num_splits = self._decode_splits(B)
+        g.num_splits = 1 if prefill_tokens else self._decode_splits(B)
         meta = make_meta(views, plan, g.num_splits)
-        meta.decode = True
+        meta.decode = not prefill_tokens
+        meta.max_q_len = prefill_tokens or 1
         meta.max_kv_len = self.config.max_model_len
         g.fbuf = torch.zeros(3, B, dtype=torch.float32, device=self.device)
         g.fbuf[1].fill_(1.0)
@@ -267,6 +284,8 @@ class ModelRunner:
 
         def body():
             h = self.model.forward(views["input_ids"], views["positions"], views["slots"], meta, kv)
+            if prefill_tokens:
+                h = h.index_select(0, views["logits_idx"].long())
             hn = self.model.final_hidden(h)
             logits = self.model.compute_logits(hn)
             ops.sample(logits, g.fbuf[0], g.ibuf, g.fbuf[1], g.fbuf[2], g.lbuf[0], g.lbuf[1], out=g.out)
@@ -315,6 +334,35 @@ class ModelRunner:
             return None
         if plan.sizes != g.sizes:
             return None
+        return self._replay(g, plan, seqs, B)
+
+    def _prefill_bucket(self, n: int) -> int:
+        cap = self.config.max_prefill_graph_tokens
+        for b in PREFILL_BUCKETS:
+            if n <= b <= cap:
+                return b
+        return -1
+
+    def _run_prefill_graph(self, seq: Sequence) -> Optional[List[int]]:
+        """Prefill of one short token run (a query or a new turn over cached
+        chunk KV) replayed from a CUDA graph captured per token bucket."""
+        n = seq.num_tokens - seq.num_cached_tokens
+        Tb = self._prefill_bucket(n) if n > 0 else -1
+        if Tb < 0:
+            return None
+        g = self.prefill_graphs.get(Tb)
+        if g is None:
+            g = self.prefill_graphs[Tb] = self._capture(1, prefill_tokens=Tb)
+        try:
+            plan = build_plan(self._items_for([seq]), self.page_size, scratch_page=self.page_manager.scratch_page,
+                              seg_cap=g.seg_cap, page_cap=g.page_cap, pad_tokens=Tb - n)
+        except OverflowError:
+            return None
+        if plan.sizes != g.sizes:
+            return None
+        return self._replay(g, plan, [seq], 1)
+
+    def _replay(self, g: _GraphSlot, plan, seqs: List[Sequence], B: int) -> List[int]:
         # Persistent pinned staging: the previous step's copies completed at its
         # token read-back, so the buffers are free to overwrite.
         if g.pin_meta is None:

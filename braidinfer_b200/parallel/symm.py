@@ -120,7 +120,8 @@ class FusedComm:
 
     # ------------------------------------------ sequence-parallel prefill
     def can_sp(self, T: int) -> bool:
-        return self.maxT < T <= self.sp_max
+        # host-tracked counters: never inside a CUDA-graph capture (NCCL there)
+        return self.maxT < T <= self.sp_max and not torch.cuda.is_current_stream_capturing()
 
     def sp_begin(self, T: int):
         """Start a sequence-parallel forward of ``T`` tokens; returns views of

@@ -1,8 +1,8 @@
 """Kernel micro-benchmarks and profiler entry points (device time, CUDA events).
 
-    python -m braidinfer_b200.utils.microbench gemm M N K [--epi 0|1] [--graph]
+    python -m braidinfer_b200.utils.microbench gemm M N K [--epi 0|1] [--graph] [--rms] [--splits S | --sweep-splits]
     python -m braidinfer_b200.utils.microbench attn-decode B L HQ HKV [--splits S]
-    python -m braidinfer_b200.utils.microbench attn-prefill L HQ HKV [--batch B]
+    python -m braidinfer_b200.utils.microbench attn-prefill L HQ HKV [--batch B] [--ctx C] [--head-dim D] [--splits S]
     python -m braidinfer_b200.utils.microbench decode-step MODEL B PROMPT_LEN
 
 ``decode-step`` runs one eager decode step of a random-init model between
@@ -54,16 +54,20 @@ def _eager_time(fn, n: int = 10) -> float:
     return a.elapsed_time(b) / n * 1e3
 
 
-def bench_gemm(M: int, N: int, K: int, epi: int = 0, graph: bool = False) -> dict:
+def bench_gemm(M: int, N: int, K: int, epi: int = 0, graph: bool = False, splits: int = -1,
+               rms: bool = False) -> dict:
     from ..ops._ext import ext
 
     x = torch.randn(M, K, device="cuda").bfloat16()
     w = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
     out = torch.empty(M, N // 2 if epi else N, device="cuda", dtype=torch.bfloat16)
-    fn = lambda: ext().gemm(out, x, w, None, None, epi, -1.0)  # noqa: E731
+    ext().gemm_force_splits(splits)
+    fn = lambda: ext().gemm(out, x, w, None, None, epi, 1e-5 if rms else -1.0)  # noqa: E731
     us = (_graph_time if graph else _eager_time)(fn)
-    return {"kernel": "gemm_tcgen05", "M": M, "N": N, "K": K, "epi": epi, "us": round(us, 2),
-            "weight_TBps": round(N * K * 2 / us / 1e6, 3), "TFLOPS": round(2 * M * N * K / us / 1e6, 1)}
+    ext().gemm_force_splits(-1)
+    return {"kernel": "gemm_tcgen05", "M": M, "N": N, "K": K, "epi": epi, "rms": rms, "splits": splits,
+            "us": round(us, 2), "weight_TBps": round(N * K * 2 / us / 1e6, 3),
+            "TFLOPS": round(2 * M * N * K / us / 1e6, 1)}
 
 
 def _decode_meta(B: int, L: int, PS: int = 256):
@@ -92,23 +96,34 @@ def bench_attn_decode(B: int, L: int, Hq: int, Hkv: int, splits: int = 0, D: int
             "us": round(us, 2), "kv_TBps": round(byts / us / 1e6, 3)}
 
 
-def bench_attn_prefill(L: int, Hq: int, Hkv: int, B: int = 1, D: int = 128) -> dict:
+def bench_attn_prefill(L: int, Hq: int, Hkv: int, B: int = 1, D: int = 128, ctx: int = 0,
+                       splits: int = 0, graph: bool = False) -> dict:
+    """Causal prefill of L query tokens per sequence; with ``ctx`` the queries
+    follow a cached segment of ctx keys (a query over cached chunks)."""
     from .. import ops
     from ..ops.attention import AttnMeta
 
     PS = 256
-    npg = -(-L // PS)
+    npg, ncg = -(-L // PS), -(-ctx // PS)
+    per = npg + ncg
     i32 = lambda v: torch.tensor(v, dtype=torch.int32, device="cuda")  # noqa: E731
-    meta = AttnMeta(qo_indptr=i32([i * L for i in range(B + 1)]), positions=i32(list(range(L)) * B),
-                    seg_indptr=i32(list(range(B + 1))), seg_page_indptr=i32([i * npg for i in range(B + 1)]),
-                    seg_offset=i32([0] * B), seg_len=i32([L] * B), seg_pos0=i32([0] * B), seg_delta=i32([0] * B),
-                    page_ids=i32(list(range(B * npg))), num_seqs=B, max_q_len=L, max_kv_len=L, decode=False)
-    kv = torch.randn(B * npg + 1, 2, Hkv, PS, D, device="cuda").bfloat16()
+    segs = 2 if ctx else 1
+    spi, soff, slen, spos0 = [0], [], [], []
+    for b in range(B):
+        if ctx:
+            spi.append(spi[-1] + ncg), soff.append(0), slen.append(ctx), spos0.append(0)
+        spi.append(spi[-1] + npg), soff.append(0), slen.append(L), spos0.append(ctx)
+    meta = AttnMeta(qo_indptr=i32([i * L for i in range(B + 1)]), positions=i32(list(range(ctx, ctx + L)) * B),
+                    seg_indptr=i32([i * segs for i in range(B + 1)]), seg_page_indptr=i32(spi),
+                    seg_offset=i32(soff), seg_len=i32(slen), seg_pos0=i32(spos0), seg_delta=i32([0] * len(slen)),
+                    page_ids=i32(list(range(B * per))), num_seqs=B, max_q_len=L, max_kv_len=L + ctx, decode=False,
+                    num_splits=splits or 1)
+    kv = torch.randn(B * per + 1, 2, Hkv, PS, D, device="cuda").bfloat16()
     q = torch.randn(B * L, Hq, D, device="cuda").bfloat16()
-    cos, sin = ops.build_cos_sin(D, 500000.0, 2 * L + 16, device="cuda")
-    us = _eager_time(lambda: ops.attention(q, kv, meta, cos, sin, D ** -0.5))
-    flops = B * 4 * L * L / 2 * Hq * D
-    return {"kernel": "attn_prefill", "L": L, "Hq": Hq, "Hkv": Hkv, "B": B, "us": round(us, 1),
+    cos, sin = ops.build_cos_sin(D, 500000.0, 2 * (L + ctx) + 16, device="cuda")
+    us = (_graph_time if graph else _eager_time)(lambda: ops.attention(q, kv, meta, cos, sin, D ** -0.5))
+    flops = B * 4 * (L * L / 2 + L * ctx) * Hq * D
+    return {"kernel": "attn_prefill", "L": L, "ctx": ctx, "Hq": Hq, "Hkv": Hkv, "D": D, "B": B, "us": round(us, 1),
             "TFLOPS_causal": round(flops / us / 1e6, 1)}
 
 
@@ -150,6 +165,9 @@ def main(argv=None) -> None:
     g.add_argument("M", type=int), g.add_argument("N", type=int), g.add_argument("K", type=int)
     g.add_argument("--epi", type=int, default=0)
     g.add_argument("--graph", action="store_true")
+    g.add_argument("--splits", type=int, default=-1, help="force the split-K factor (-1: heuristic)")
+    g.add_argument("--rms", action="store_true", help="fused input RMSNorm")
+    g.add_argument("--sweep-splits", action="store_true", help="time every split-K factor 1..16")
     a = sub.add_parser("attn-decode")
     for n in ("B", "L", "Hq", "Hkv"):
         a.add_argument(n, type=int)
@@ -158,15 +176,24 @@ def main(argv=None) -> None:
     for n in ("L", "Hq", "Hkv"):
         p.add_argument(n, type=int)
     p.add_argument("--batch", type=int, default=1)
+    p.add_argument("--ctx", type=int, default=0, help="cached keys before the queries")
+    p.add_argument("--head-dim", type=int, default=128)
+    p.add_argument("--splits", type=int, default=0, help="force key splits (0: automatic)")
+    p.add_argument("--graph", action="store_true", help="time 20 launches replayed from a CUDA graph")
     s = sub.add_parser("decode-step")
     s.add_argument("model"), s.add_argument("B", type=int), s.add_argument("plen", type=int)
     args = ap.parse_args(argv)
     if args.cmd == "gemm":
-        print(json.dumps(bench_gemm(args.M, args.N, args.K, args.epi, args.graph)))
+        if args.sweep_splits:
+            for sp in (0, 1, 2, 3, 4, 6, 8, 12, 16):
+                print(json.dumps(bench_gemm(args.M, args.N, args.K, args.epi, args.graph, sp, args.rms)))
+        else:
+            print(json.dumps(bench_gemm(args.M, args.N, args.K, args.epi, args.graph, args.splits, args.rms)))
     elif args.cmd == "attn-decode":
         print(json.dumps(bench_attn_decode(args.B, args.L, args.Hq, args.Hkv, args.splits)))
     elif args.cmd == "attn-prefill":
-        print(json.dumps(bench_attn_prefill(args.L, args.Hq, args.Hkv, args.batch)))
+        print(json.dumps(bench_attn_prefill(args.L, args.Hq, args.Hkv, args.batch, args.head_dim, args.ctx,
+                                            args.splits, args.graph)))
     else:
         decode_step(args.model, args.B, args.plen)
         print("decode step done")

@@ -357,29 +357,42 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(const __grid_consta
       {
         // query rows rotated for this segment: one position for every row,
         // all loads independent (issued together)
-        constexpr int H2 = D / 2;
+        // (one item = 8 dims of each rotary half of one row, 16-byte accesses)
+        constexpr int H2 = D / 2, CH = H2 / 8;
         int pos = qpos - p.seg_delta[s];
         pos = pos < 0 ? 0 : (pos >= p.rope_len ? p.rope_len - 1 : pos);
-        __nv_bfloat16* qt = reinterpret_cast<__nv_bfloat16*>(qs);
-#pragma unroll
-        for (int k = 0; k < 16 * H2 / 128; ++k) {
-          const int i = threadIdx.x + 128 * k;
-          const int r = i / H2, d = i % H2;
-          float x1 = 0.f, x2 = 0.f;
+        if (threadIdx.x < 16 * CH) {
+          const int r = threadIdx.x / CH, c8 = (threadIdx.x % CH) * 8;
+          uint4 o1 = make_uint4(0, 0, 0, 0), o2 = make_uint4(0, 0, 0, 0);
           if (r < G) {
             const __nv_bfloat16* qp = p.q + ((size_t)t * p.Hq + kh * G + r) * D;
-            const float a = bf2f(qp[d]), bb = bf2f(qp[d + H2]);
+            const uint4 a4 = *reinterpret_cast<const uint4*>(qp + c8);
+            const uint4 b4 = *reinterpret_cast<const uint4*>(qp + H2 + c8);
             if (p.use_rope) {
-              const float cs = p.cos[(size_t)pos * H2 + d], sn = p.sin[(size_t)pos * H2 + d];
-              x1 = a * cs - bb * sn;
-              x2 = bb * cs + a * sn;
+              const float* cp = p.cos + (size_t)pos * H2 + c8;
+              const float* sp = p.sin + (size_t)pos * H2 + c8;
+              float cs[8], sn[8];
+              *reinterpret_cast<float4*>(cs) = *reinterpret_cast<const float4*>(cp);
+              *reinterpret_cast<float4*>(cs + 4) = *reinterpret_cast<const float4*>(cp + 4);
+              *reinterpret_cast<float4*>(sn) = *reinterpret_cast<const float4*>(sp);
+              *reinterpret_cast<float4*>(sn + 4) = *reinterpret_cast<const float4*>(sp + 4);
+              const __nv_bfloat16* a = reinterpret_cast<const __nv_bfloat16*>(&a4);
+              const __nv_bfloat16* bb = reinterpret_cast<const __nv_bfloat16*>(&b4);
+              __nv_bfloat16* y1 = reinterpret_cast<__nv_bfloat16*>(&o1);
+              __nv_bfloat16* y2 = reinterpret_cast<__nv_bfloat16*>(&o2);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const float x1 = bf2f(a[j]), x2 = bf2f(bb[j]);
+                y1[j] = f2bf(x1 * cs[j] - x2 * sn[j]);
+                y2[j] = f2bf(x2 * cs[j] + x1 * sn[j]);
+              }
             } else {
-              x1 = a;
-              x2 = bb;
+              o1 = a4;
+              o2 = b4;
             }
           }
-          qt[(tswz<16>(r, d / 8) >> 1) + (d & 7)] = f2bf(x1);
-          qt[(tswz<16>(r, (d + H2) / 8) >> 1) + ((d + H2) & 7)] = f2bf(x2);
+          *reinterpret_cast<uint4*>(qs + tswz<16>(r, c8 / 8)) = o1;
+          *reinterpret_cast<uint4*>(qs + tswz<16>(r, (H2 + c8) / 8)) = o2;
         }
       }
       __syncthreads();
@@ -550,11 +563,14 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(const __grid_consta
 }
 
 // -------------------------------------------------------------- prefill
-// Prefill (or chunk self-prefill) attention: grid (64-row q tile, seq, kv
-// head); rows are (token, head-in-group) pairs.  Warp 0 streams 64-key K/V
-// tiles with TMA into a STAGES-deep mbarrier ring (as in decode) while each
-// warp computes its 16 rows against every tile; tiles past the last query
-// position of this q tile are not loaded.
+// Prefill (or chunk self-prefill) attention: grid (64-row q tile, seq,
+// kv head x splits); rows are (token, head-in-group) pairs.  Warp 0 streams
+// 64-key K/V tiles with TMA into a STAGES-deep mbarrier ring (as in decode)
+// while each warp computes its 16 rows against every tile; keys past the last
+// query position of the q tile are never loaded.  With num_splits > 1 (a short
+// query over long cached chunks: few q tiles) the visible keys are divided
+// into contiguous ranges, one per CTA; each CTA writes its normalised partial
+// and log-sum-exp and the last CTA of the q tile merges them.
 template <int D, int STAGES, int BR>
 __global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const __grid_constant__ CUtensorMap tmkv,
                                                               const AttnParams p) {
@@ -566,7 +582,9 @@ __global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const __grid_const
   uint8_t* qs = vbuf + STAGES * TILE;  // [64][D], tswz<64>
   uint64_t* full = reinterpret_cast<uint64_t*>(qs + 64 * D * 2);
   uint64_t* empty = full + STAGES;
-  const int b = blockIdx.y, kh = blockIdx.z;
+  __shared__ int s_last;
+  const int S = p.num_splits;
+  const int b = blockIdx.y, kh = blockIdx.z / S, split = blockIdx.z % S;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmkv);
@@ -579,6 +597,9 @@ __global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const __grid_const
   __syncthreads();
   pdl_wait();
   pdl_trigger();
+  unsigned long long* tr = p.trace
+      ? p.trace + 8 * ((size_t)(blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) : nullptr;
+  if (tr != nullptr && threadIdx.x == 0) tr[0] = globaltimer_ns();
   const int G = p.G;
   const int t0 = p.qo_indptr[b], nt = p.qo_indptr[b + 1] - t0;
   const int rows = nt * G;
@@ -595,28 +616,41 @@ __global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const __grid_const
     rpos[h] = rr < rows ? p.positions[t0 + rr / G] : -1;
   }
   const int s0 = p.seg_indptr[b], s1 = p.seg_indptr[b + 1];
-  // restrict each segment to keys that some row of this tile can see
+  // keys some row of this tile can see: a prefix of each segment
+  auto seg_vis = [&](int s) { return max(0, min(p.seg_len[s], max_pos - p.seg_pos0[s] + 1)); };
+  // this split's range [r0, r1) of the concatenated visible keys
+  int r0 = 0, r1 = 1 << 30;
+  if (S > 1) {
+    int total = 0;
+    for (int s = s0; s < s1; ++s) total += seg_vis(s);
+    const int per = ((total + S - 1) / S + KT - 1) / KT * KT;
+    r0 = min(total, split * per);
+    r1 = min(total, r0 + per);
+  }
+  // producer cursor (warp 0): segment s, keys [lo, hi) of it, next tile sl
   ProdCursor pc{s0, s1, 0, 0, 0, 0, 0, 0, 0, 0, nullptr};
-  auto seg_hi = [&](int s, int len) { return min(len, max_pos - p.seg_pos0[s] + 1); };
+  int pc_vis = 0;
   auto settle = [&]() {
     while (pc.s < pc.s1) {
-      const int len = p.seg_len[pc.s];
-      pc.lo = 0;
-      pc.hi = seg_hi(pc.s, len);
-      if (pc.hi > 0) {
+      pc_vis = seg_vis(pc.s);
+      pc.lo = max(0, r0 - pc.segstart);
+      pc.hi = min(pc_vis, r1 - pc.segstart);
+      if (pc.lo < pc.hi) {
         pc.off = p.seg_offset[pc.s];
         pc.pages = p.page_ids + p.seg_page_indptr[pc.s];
         pc.npages = p.seg_page_indptr[pc.s + 1] - p.seg_page_indptr[pc.s];
-        pc.sl = pc.off & ~(KT - 1);
+        pc.sl = (pc.off + pc.lo) & ~(KT - 1);
         pc.win = -(1 << 30);
         return;
       }
+      pc.segstart += pc_vis;
       ++pc.s;
     }
   };
   auto advance = [&]() {
     pc.sl += KT;
     if (pc.sl < pc.off + pc.hi) return;
+    pc.segstart += pc_vis;
     ++pc.s;
     settle();
   };
@@ -658,41 +692,59 @@ __global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const __grid_const
   uint32_t qf[D / 16][4];
   int it = 0;
   bool ok = true;
+  int segstart = 0;
   // every warp runs the same segment iterations (and so the same barriers),
   // even after a timed-out wait has stopped its tile loop
   for (int s = s0; s < s1; ++s) {
-    const int len = p.seg_len[s];
     const int pos0 = p.seg_pos0[s];
-    const int hi = seg_hi(s, len);
-    if (hi <= 0) continue;
+    const int vis = seg_vis(s);
+    const int lo = max(0, r0 - segstart), hi = min(vis, r1 - segstart);
+    segstart += vis;
+    if (lo >= hi) continue;
     __syncthreads();
     {
-      constexpr int H2 = D / 2;
+      // Rotated query tile: one item = 8 dims of each rotary half of one row
+      // (16-byte q loads, 32-byte cos/sin loads, 16-byte swizzled smem stores).
+      constexpr int H2 = D / 2, CH = H2 / 8;
       const int delta = p.seg_delta[s];
-      __nv_bfloat16* qt = reinterpret_cast<__nv_bfloat16*>(qs);
-#pragma unroll 4
-      for (int k = 0; k < 64 * H2 / 128; ++k) {
+#pragma unroll
+      for (int k = 0; k < 64 * CH / 128; ++k) {
         const int i = threadIdx.x + 128 * k;
-        const int r = i / H2, d = i % H2;
-        float x1 = 0.f, x2 = 0.f;
+        const int r = i / CH, c8 = (i % CH) * 8;
+        uint4 o1 = make_uint4(0, 0, 0, 0), o2 = make_uint4(0, 0, 0, 0);
         if (r < nrows) {
           const int rr = row0 + r;
           const int tok = t0 + rr / G, g = rr % G;
           const __nv_bfloat16* qp = p.q + ((size_t)tok * p.Hq + kh * G + g) * D;
-          const float a = bf2f(qp[d]), bb = bf2f(qp[d + H2]);
+          const uint4 a4 = *reinterpret_cast<const uint4*>(qp + c8);
+          const uint4 b4 = *reinterpret_cast<const uint4*>(qp + H2 + c8);
           if (p.use_rope) {
             int pos = p.positions[tok] - delta;
             pos = pos < 0 ? 0 : (pos >= p.rope_len ? p.rope_len - 1 : pos);
-            const float cs = p.cos[(size_t)pos * H2 + d], sn = p.sin[(size_t)pos * H2 + d];
-            x1 = a * cs - bb * sn;
-            x2 = bb * cs + a * sn;
+            const float* cp = p.cos + (size_t)pos * H2 + c8;
+            const float* sp = p.sin + (size_t)pos * H2 + c8;
+            float cs[8], sn[8];
+            *reinterpret_cast<float4*>(cs) = *reinterpret_cast<const float4*>(cp);
+            *reinterpret_cast<float4*>(cs + 4) = *reinterpret_cast<const float4*>(cp + 4);
+            *reinterpret_cast<float4*>(sn) = *reinterpret_cast<const float4*>(sp);
+            *reinterpret_cast<float4*>(sn + 4) = *reinterpret_cast<const float4*>(sp + 4);
+            const __nv_bfloat16* a = reinterpret_cast<const __nv_bfloat16*>(&a4);
+            const __nv_bfloat16* bb = reinterpret_cast<const __nv_bfloat16*>(&b4);
+            __nv_bfloat16* y1 = reinterpret_cast<__nv_bfloat16*>(&o1);
+            __nv_bfloat16* y2 = reinterpret_cast<__nv_bfloat16*>(&o2);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float x1 = bf2f(a[j]), x2 = bf2f(bb[j]);
+              y1[j] = f2bf(x1 * cs[j] - x2 * sn[j]);
+              y2[j] = f2bf(x2 * cs[j] + x1 * sn[j]);
+            }
           } else {
-            x1 = a;
-            x2 = bb;
+            o1 = a4;
+            o2 = b4;
           }
         }
-        qt[(tswz<64>(r, d / 8) >> 1) + (d & 7)] = f2bf(x1);
-        qt[(tswz<64>(r, (d + H2) / 8) >> 1) + ((d + H2) & 7)] = f2bf(x2);
+        *reinterpret_cast<uint4*>(qs + tswz<64>(r, c8 / 8)) = o1;
+        *reinterpret_cast<uint4*>(qs + tswz<64>(r, (H2 + c8) / 8)) = o2;
       }
     }
     __syncthreads();
@@ -702,8 +754,9 @@ __global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const __grid_const
       for (int kk = 0; kk < D / 16; ++kk)
         ldsm_x4(smem_u32(qs) + tswz<64>(r, kk * 2 + (lane >> 4)), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
     }
+    if (tr != nullptr && threadIdx.x == 0 && tr[1] == 0) tr[1] = globaltimer_ns();
     const int off = p.seg_offset[s];
-    for (int sl = off & ~(KT - 1); sl < off + hi && ok; sl += KT, ++it) {
+    for (int sl = (off + lo) & ~(KT - 1); sl < off + hi && ok; sl += KT, ++it) {
       if (warp == 0 && pc.s < pc.s1) {
         const int st2 = issued % STAGES;
         int okw = 1;
@@ -740,15 +793,15 @@ __global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const __grid_const
         }
       }
       const int j0 = sl - off;
-      const bool need_mask = (pos0 + j0 + KT - 1 > min_pos) || j0 < 0 || (j0 + KT > hi);
+      const bool need_mask = (pos0 + j0 + KT - 1 > min_pos) || j0 < lo || (j0 + KT > hi);
       if (need_mask) {
 #pragma unroll
         for (int nb = 0; nb < 8; ++nb)
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int j = j0 + nb * 8 + 2 * (lane & 3) + (e & 1);
-            const bool vis = j >= 0 && j < hi && pos0 + j <= rpos[e >> 1];
-            sc[nb][e] = vis ? sc[nb][e] * p.scale_log2 : -INFINITY;
+            const bool v = j >= lo && j < hi && pos0 + j <= rpos[e >> 1];
+            sc[nb][e] = v ? sc[nb][e] * p.scale_log2 : -INFINITY;
           }
       } else {
 #pragma unroll
@@ -777,29 +830,131 @@ __global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const __grid_const
       if (lane == 0) mbar_arrive(&empty[st]);
     }
   }
-  // ---- normalise and store
   const int c = lane & 3;
+  if (tr != nullptr && threadIdx.x == 0) tr[2] = globaltimer_ns();
+  if (S == 1) {
+    // ---- normalise and store
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int rr = row0 + warp * 16 + gq + 8 * h;
+      if (rr >= rows) continue;
+      const int tok = t0 + rr / G, head = kh * G + rr % G;
+      const float inv = l[h] > 0.f ? 1.f / l[h] : 0.f;
+      __nv_bfloat16* o = p.out + (size_t)tok * p.Hq * D + head * D;
+#pragma unroll
+      for (int nb = 0; nb < D / 8; ++nb) {
+        const int d = nb * 8 + 2 * c;
+        *reinterpret_cast<__nv_bfloat162*>(o + d) =
+            __floats2bfloat162_rn(acc[nb][2 * h] * inv, acc[nb][2 * h + 1] * inv);
+      }
+    }
+    return;
+  }
+  // ---- split: publish this CTA's partial, the last CTA of the q tile merges
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     const int rr = row0 + warp * 16 + gq + 8 * h;
     if (rr >= rows) continue;
     const int tok = t0 + rr / G, head = kh * G + rr % G;
+    const size_t idx = ((size_t)tok * p.Hq + head) * S + split;
     const float inv = l[h] > 0.f ? 1.f / l[h] : 0.f;
-    __nv_bfloat16* o = p.out + (size_t)tok * p.Hq * D + head * D;
+    float* po = p.part_o + idx * D;
 #pragma unroll
-    for (int nb = 0; nb < D / 8; ++nb) {
-      const int d = nb * 8 + 2 * c;
-      *reinterpret_cast<__nv_bfloat162*>(o + d) = __floats2bfloat162_rn(acc[nb][2 * h] * inv, acc[nb][2 * h + 1] * inv);
+    for (int nb = 0; nb < D / 8; ++nb)
+      *reinterpret_cast<float2*>(po + nb * 8 + 2 * c) = make_float2(acc[nb][2 * h] * inv, acc[nb][2 * h + 1] * inv);
+    if (c == 0) p.part_lse[idx] = l[h] > 0.f ? m[h] + log2f(l[h]) : -INFINITY;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int* ctr = p.counters + ((size_t)b * p.Hkv + kh) * gridDim.x + blockIdx.x;
+    // releases this CTA's partial, acquires the other splits' partials
+    const int old = atomic_add_acq_rel_gpu(ctr, 1);
+    s_last = old == S - 1;
+    if (s_last) *ctr = 0;
+  }
+  __syncthreads();
+  if (tr != nullptr && threadIdx.x == 0) tr[3] = globaltimer_ns();
+  if (!s_last) return;
+  // merge weights per row in shared memory (the K ring is idle now); every
+  // lse / partial load of a row is issued before any is used
+  float* wsm = reinterpret_cast<float*>(kbuf);  // [64][S]
+  if (threadIdx.x < nrows) {
+    const int rr = row0 + threadIdx.x;
+    const size_t base = (((size_t)(t0 + rr / G)) * p.Hq + kh * G + rr % G) * S;
+    float lse[32];
+#pragma unroll
+    for (int q = 0; q < 32; ++q) lse[q] = q < S ? __ldcg(p.part_lse + base + q) : -INFINITY;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < 32; ++q) mx = fmaxf(mx, lse[q]);
+    float sum = 0.f;
+#pragma unroll
+    for (int q = 0; q < 32; ++q) {
+      lse[q] = (mx == -INFINITY || q >= S) ? 0.f : exp2f(lse[q] - mx);
+      sum += lse[q];
+    }
+    const float inv = sum > 0.f ? 1.f / sum : 0.f;
+#pragma unroll
+    for (int q = 0; q < 32; ++q)
+      if (q < S) wsm[threadIdx.x * S + q] = lse[q] * inv;
+  }
+  __syncthreads();
+  constexpr int C4 = D / 4;
+  for (int i0 = threadIdx.x; i0 < nrows * C4; i0 += 256) {
+    // two output float4s per thread per pass, 8 splits of each in flight
+    float4 o4[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+    size_t pb[2];
+    int rr_[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int i = min(i0 + 128 * u, nrows * C4 - 1);
+      const int r = i / C4, d = (i % C4) * 4;
+      const int rr = row0 + r;
+      rr_[u] = r;
+      pb[u] = (((size_t)(t0 + rr / G)) * p.Hq + kh * G + rr % G) * S * D + d;
+    }
+    for (int q0 = 0; q0 < S; q0 += 8) {
+      float4 v[2][8];
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          v[u][k] = q0 + k < S ? __ldcg(reinterpret_cast<const float4*>(p.part_o + pb[u] + (size_t)(q0 + k) * D))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float w = q0 + k < S ? wsm[rr_[u] * S + q0 + k] : 0.f;
+          o4[u].x += w * v[u][k].x;
+          o4[u].y += w * v[u][k].y;
+          o4[u].z += w * v[u][k].z;
+          o4[u].w += w * v[u][k].w;
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int i = i0 + 128 * u;
+      if (i >= nrows * C4) continue;
+      const int r = i / C4, d = (i % C4) * 4;
+      const int rr = row0 + r;
+      const int tok = t0 + rr / G, head = kh * G + rr % G;
+      __nv_bfloat16* o = p.out + (size_t)tok * p.Hq * D + head * D + d;
+      *reinterpret_cast<__nv_bfloat162*>(o) = __floats2bfloat162_rn(o4[u].x, o4[u].y);
+      *reinterpret_cast<__nv_bfloat162*>(o + 2) = __floats2bfloat162_rn(o4[u].z, o4[u].w);
     }
   }
+  if (tr != nullptr && threadIdx.x == 0) tr[4] = globaltimer_ns();
 }
 
 // ------------------------------------------------------------------ host
 static unsigned long long* g_attn_trace = nullptr;
-// Profiling: per-CTA phase timestamps of subsequent decode launches (int64 [8 * CTAs]).
+// Profiling: per-CTA phase timestamps of subsequent attention launches (int64 [8 * CTAs]).
 void attn_set_trace(torch::Tensor buf) {
   g_attn_trace = buf.defined() && buf.numel() ? reinterpret_cast<unsigned long long*>(buf.data_ptr<int64_t>()) : nullptr;
 }
+
+int gemm_num_sms();
 
 // Per-device split-merge counters (zeroed once; the merging CTA re-arms its counter).
 static int* attn_counters(int dev, size_t n) {
@@ -858,7 +1013,7 @@ static void launch_attn(AttnParams& p, int num_seqs, int max_q_len, bool decode,
         attr = true;
       }
       CUtensorMap tm = make_tmap(p.kv, rows, D, D, 64);
-      launch_pdl(k, dim3(qt, num_seqs, p.Hkv), dim3(128), smem, st, tm, p);
+      launch_pdl(k, dim3(qt, num_seqs, p.Hkv * p.num_splits), dim3(128), smem, st, tm, p);
     } else {
       auto k = attn_prefill_kernel<D, STAGES, 16>;
       static bool attr = false;
@@ -867,7 +1022,7 @@ static void launch_attn(AttnParams& p, int num_seqs, int max_q_len, bool decode,
         attr = true;
       }
       CUtensorMap tm = make_tmap(p.kv, rows, D, D, 16);
-      launch_pdl(k, dim3(qt, num_seqs, p.Hkv), dim3(128), smem, st, tm, p);
+      launch_pdl(k, dim3(qt, num_seqs, p.Hkv * p.num_splits), dim3(128), smem, st, tm, p);
     }
   }
 }
@@ -911,8 +1066,27 @@ void attention(torch::Tensor out, torch::Tensor q, torch::Tensor kv, torch::Tens
   p.Hkv = Hkv;
   p.G = G;
   p.PS = PS;
-  p.num_splits = decode ? (int)std::max<int64_t>(1, num_splits) : 1;
-  p.trace = decode ? g_attn_trace : nullptr;
+  size_t n_counters = (size_t)T * Hkv;
+  if (decode) {
+    p.num_splits = (int)std::max<int64_t>(1, num_splits);
+  } else {
+    // Prefill: split the keys when the q tiles alone leave SMs idle (a short
+    // query over long cached chunks); each split keeps >= 2 key tiles.
+    const int qt = (int)((max_q_len * G + 63) / 64);
+    const int64_t work = (int64_t)qt * num_seqs * Hkv;
+    static const int forced = [] {  // tuning knob: BRAID_PREFILL_SPLITS=n
+      const char* e = getenv("BRAID_PREFILL_SPLITS");
+      return e ? atoi(e) : 0;
+    }();
+    int ns = 1;
+    const int sms = gemm_num_sms();
+    if (work < sms) ns = (int)std::min<int64_t>({(2 * sms + work - 1) / work, 32, std::max<int64_t>(1, max_kv_len / 128)});
+    if (num_splits > 1) ns = (int)std::min<int64_t>(num_splits, 32);
+    if (forced > 0) ns = std::min(forced, 32);
+    p.num_splits = std::max(1, ns);
+    n_counters = (size_t)qt * num_seqs * Hkv;
+  }
+  p.trace = g_attn_trace;
   torch::Tensor po, pl;
   if (p.num_splits > 1) {
     if (part_o.has_value() && part_o->defined() && part_o->numel() >= (int64_t)T * Hq * p.num_splits * D) {
@@ -924,7 +1098,7 @@ void attention(torch::Tensor out, torch::Tensor q, torch::Tensor kv, torch::Tens
     }
     p.part_o = po.data_ptr<float>();
     p.part_lse = pl.data_ptr<float>();
-    p.counters = attn_counters(q.get_device(), (size_t)T * Hkv);
+    p.counters = attn_counters(q.get_device(), n_counters);
   }
   if (D == 128)
     launch_attn<128>(p, num_seqs, max_q_len, decode, T, kv.size(0), st);

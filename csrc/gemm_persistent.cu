@@ -212,11 +212,17 @@ __global__ void row_rstd_kernel(const __nv_bfloat16* __restrict__ x, int ld, int
   if (row >= T) return;
   const __nv_bfloat16* xr = x + (size_t)row * ld;
   float ss = 0.f;
-  for (int k = lane * 8; k < K; k += 256) {
-    const uint4 u = *reinterpret_cast<const uint4*>(xr + k);
-    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+  for (int k0 = lane * 8; k0 < K; k0 += 256 * 8) {
+    uint4 u[8];  // 8 loads in flight per lane
 #pragma unroll
-    for (int j = 0; j < 8; ++j) ss += bf2f(e[j]) * bf2f(e[j]);
+    for (int i = 0; i < 8; ++i)
+      u[i] = k0 + 256 * i < K ? *reinterpret_cast<const uint4*>(xr + k0 + 256 * i) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += bf2f(e[j]) * bf2f(e[j]);
+    }
   }
   ss = warp_sum(ss);
   if (lane == 0) out[row] = rsqrtf(ss / K + eps);

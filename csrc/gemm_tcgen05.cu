@@ -204,39 +204,42 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
   } else {
     // ------------------------------------------------------------ epilogue
     pdl_wait();
-    // Fused input RMSNorm: 1/rms of every token of the tile (overlaps the mainloop).
-    if (args.rs_x != nullptr) {
-      if (args.swap) {
-        for (int tt = ew; tt < BN; tt += 4) {
-          const int t = n0 + tt;
-          float ss = 0.f;
-          if (t < args.N) {
+    // Fused input RMSNorm (swapped mode): 1/rms of every token of the tile,
+    // overlapping the mainloop.  Two tokens per warp iteration with up to 16
+    // 16-byte loads in flight per lane (one memory round trip per 2K columns).
+    // Normal mode receives the values precomputed in rs_vec.
+    if (args.rs_x != nullptr && args.swap) {
+      for (int tt = ew; tt < BN; tt += 8) {
+        float ss[2] = {0.f, 0.f};
+        const int t0 = n0 + tt;
+        for (int k0 = lane * 8; k0 < args.K; k0 += 256 * 8) {
+          uint4 u[2][8];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int t = t0 + 4 * h;
+            const bool live = tt + 4 * h < BN && t < args.N;
             const __nv_bfloat16* xr = args.rs_x + (size_t)t * args.rs_ld;
-            for (int k = lane * 8; k < args.K; k += 256) {
-              const uint4 u = *reinterpret_cast<const uint4*>(xr + k);
-              const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
 #pragma unroll
-              for (int j = 0; j < 8; ++j) ss += bf2f(e[j]) * bf2f(e[j]);
+            for (int i = 0; i < 8; ++i)
+              u[h][i] = (live && k0 + 256 * i < args.K) ? *reinterpret_cast<const uint4*>(xr + k0 + 256 * i)
+                                                         : make_uint4(0, 0, 0, 0);
+          }
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u[h][i]);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) ss[h] += bf2f(e[j]) * bf2f(e[j]);
             }
-          }
-          ss = warp_sum(ss);
-          if (lane == 0) rstd_s[tt] = rsqrtf(ss / args.K + args.rs_eps);
         }
-        named_bar_sync(1, 128);
-      } else {
-        const int m = m0 + r;
-        if (m < args.M) {
-          const __nv_bfloat16* xr = args.rs_x + (size_t)m * args.rs_ld;
-          float ss = 0.f;
-          for (int k = 0; k < args.K; k += 8) {
-            const uint4 u = *reinterpret_cast<const uint4*>(xr + k);
-            const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) ss += bf2f(e[j]) * bf2f(e[j]);
-          }
-          rs_row = rsqrtf(ss / args.K + args.rs_eps);
+        for (int h = 0; h < 2; ++h) {
+          const float v = warp_sum(ss[h]);
+          if (lane == 0 && tt + 4 * h < BN) rstd_s[tt + 4 * h] = rsqrtf(v / args.K + args.rs_eps);
         }
       }
+      named_bar_sync(1, 128);
     }
     const bool ready = mbar_wait(tmem_full, 0);
     if (!ready) atomicExch(args.err, 3);
@@ -271,7 +274,9 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
     // Split-K (global path): publish this slice's partial, elect the last CTA of the tile.
     bool last = args.cluster ? cluster_rank() == 0 : true;
     if (args.splits > 1 && !args.cluster) {
-      float* mine = args.ws + ((size_t)(tile * args.splits + split) * BM + r) * BN;
+      // Partial tile layout [BN/4][BM] float4: a warp's 32 rows of one 4-column
+      // chunk are 512 contiguous bytes, so publishing and summing coalesce.
+      float* mine = args.ws + (size_t)(tile * args.splits + split) * BM * BN;
       for (int c0 = 0; c0 < BN; c0 += 16) {
         float v[16];
         if (has_acc) {
@@ -283,7 +288,8 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
         }
 #pragma unroll
         for (int j = 0; j < 16; j += 4)
-          *reinterpret_cast<float4*>(mine + c0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+          *reinterpret_cast<float4*>(mine + ((size_t)((c0 + j) >> 2) * BM + r) * 4) =
+              make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
       }
       named_bar_sync(1, 128);
       if (et == 0) {
@@ -326,9 +332,10 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
 #pragma unroll
             for (int q = 0; q < 8; ++q)
               if (s0 + q < args.splits) {
-                const float* p = args.ws + ((size_t)(tile * args.splits + s0 + q) * BM + r) * BN + c0;
+                const float* p = args.ws + (size_t)(tile * args.splits + s0 + q) * BM * BN;
 #pragma unroll
-                for (int j = 0; j < 4; ++j) f[q][j] = __ldcg(reinterpret_cast<const float4*>(p + 4 * j));
+                for (int j = 0; j < 4; ++j)
+                  f[q][j] = __ldcg(reinterpret_cast<const float4*>(p + ((size_t)((c0 >> 2) + j) * BM + r) * 4));
               }
 #pragma unroll
             for (int q = 0; q < 8; ++q)
@@ -598,6 +605,10 @@ int gemm_num_sms() {
   return n;
 }
 
+static int g_forced_splits = -1;
+// Tuning: force the split-K factor of later tile-per-CTA launches (0 = heuristic, -1 = environment).
+void gemm_force_splits(int64_t n) { g_forced_splits = (int)n; }
+
 static unsigned long long* g_trace = nullptr;
 // Profiling: record per-CTA phase timestamps of subsequent GEMM launches into
 // `buf` (int64 [8 * CTAs]); an empty tensor switches recording off.
@@ -697,15 +708,29 @@ static int64_t run_gemm(GemmArgs& a, const torch::Tensor& x, const torch::Tensor
     launch_gemm_persistent(ta, tb, a, BN, st);
     return arrivals;
   }
+  torch::Tensor rstd_tmp;
+  if (!swap && a.rs_x != nullptr && a.rs_vec == nullptr) {
+    rstd_tmp = torch::empty({T}, x.options().dtype(at::kFloat));
+    launch_row_rstd(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), T, K, a.rs_eps,
+                    rstd_tmp.data_ptr<float>(), st);
+    a.rs_vec = rstd_tmp.data_ptr<float>();
+  }
   if (a.rs_vec != nullptr) a.rs_x = nullptr;
   // Split-K so that one wave of resident CTAs (2 per SM for decode tiles)
   // covers the machine; decode shapes have few output tiles.
   int splits = 1;
   const int slots = gemm_num_sms() * (swap ? 2 : 1);
   if (tiles < slots) splits = std::max(1, std::min({slots / tiles, kb_total / 2, 16}));
-  static const int forced = [] {  // tuning knob: BRAID_GEMM_SPLITS=n forces the split-K factor
-    const char* e = getenv("BRAID_GEMM_SPLITS");
-    return e ? atoi(e) : 0;
+  // The last CTA of a tile sums splits x BM x BN fp32 partials alone; past
+  // 256 partial columns that tail outweighs the shorter K loop (measured on
+  // B200 over decode and short-prefill shapes: BN 64 is best at 1-4 splits).
+  splits = std::max(1, std::min(splits, 256 / BN));
+  const int forced = g_forced_splits >= 0 ? g_forced_splits : [] {  // BRAID_GEMM_SPLITS=n forces the factor
+    static const int env = [] {
+      const char* e = getenv("BRAID_GEMM_SPLITS");
+      return e ? atoi(e) : 0;
+    }();
+    return env;
   }();
   if (forced > 0) splits = std::max(1, std::min(forced, kb_total));
   int kbps = (kb_total + splits - 1) / splits;

@@ -61,3 +61,27 @@ def test_chunked_cascade_gpu(ckpt):
         outs.append((o["token_ids"], m.llm.model_runner.capture_logits[0][0]))
     d = (outs[0][1] - outs[1][1]).abs().max().item()
     assert d < 0.05 * outs[1][1].abs().max().item() + 0.02, d
+
+
+def test_prefill_graph_matches_eager(ckpt):
+    """Single-sequence prefills up to max_prefill_graph_tokens replay a CUDA
+    graph (token count padded to a bucket); outputs equal the eager engine."""
+    from braidinfer_b200 import ChunkType, ChunkedLLM
+    g = torch.Generator().manual_seed(5)
+    rnd = lambda n: torch.randint(3, 1024, (n,), generator=g).tolist()  # noqa: E731
+    sys_t, ctx_t = rnd(40), [rnd(70), rnd(33)]
+    queries = [rnd(n) for n in (5, 16, 40, 100, 200)]
+    sp = dict(temperature=0, max_tokens=5, ignore_eos=True)
+    res = []
+    for eager in (True, False):
+        cl = ChunkedLLM(ckpt, num_kvcache_blocks=96, kvcache_block_size=16, enforce_eager=eager, max_graph_batch=4)
+        s = cl.register_chunk("s", ChunkType.SYSTEM_PROMPT, token_ids=sys_t)
+        cs = [cl.register_chunk(f"c{i}", ChunkType.CONTEXT, token_ids=t) for i, t in enumerate(ctx_t)]
+        outs = []
+        for i, qt in enumerate(queries):
+            q = cl.register_chunk(f"q{i}", ChunkType.QUERY, token_ids=qt)
+            outs.append(cl.generate_from_chunks(s, q, cs, sp)["token_ids"])
+        if not eager:
+            assert len(cl.llm.model_runner.prefill_graphs) >= 3
+        res.append(outs)
+    assert res[0] == res[1]

@@ -256,13 +256,32 @@ def test_attention_decode(D, G, splits):
 
 
 @pytest.mark.parametrize("D,G", [(64, 8), (128, 2), (128, 4)])
-def test_attention_prefill(D, G):
+@pytest.mark.parametrize("splits", [1, 3, 7])
+def test_attention_prefill(D, G, splits):
+    """splits > 1: keys divided over CTAs, partials merged by the last CTA."""
     from braidinfer_b200 import ops
     PS, P, Hkv = 16, 1024, 2
     Hq = Hkv * G
     # (q_len, segments): last segment is the private one holding the queries
     seqs = [(50, [(40, 0, 3), (70, 5, -11), (50, 0, 0)]), (1, [(1, 0, 0)]), (200, [(200, 0, 0)]),
             (17, [(128, 0, 0), (33, 0, 0)])]
+    meta, T = _rand_plan(seqs, PS, P, DEV, False)
+    meta.num_splits = splits
+    kv = torch.randn(P, 2, Hkv, PS, D, device=DEV).bfloat16()
+    q = torch.randn(T, Hq, D, device=DEV).bfloat16()
+    cos, sin = ops.build_cos_sin(D, 10000.0, 2048, device=DEV)
+    out = ops.attention(q, kv, meta, cos, sin, D ** -0.5, True)
+    ref = ops.attention_ref(q.cpu().float(), kv.cpu().float(), meta, cos.cpu(), sin.cpu(), D ** -0.5, True)
+    torch.testing.assert_close(out.float().cpu(), ref.float(), atol=2e-2, rtol=2e-2)
+
+
+@pytest.mark.parametrize("D,G", [(64, 8), (128, 4)])
+def test_attention_prefill_short_query_long_context(D, G):
+    """A short query over long cached chunks picks key splits automatically."""
+    from braidinfer_b200 import ops
+    PS, P, Hkv = 16, 1024, 2
+    Hq = Hkv * G
+    seqs = [(20, [(300, 0, 4), (500, 7, -3), (129, 3, 9), (20, 0, 0)])]
     meta, T = _rand_plan(seqs, PS, P, DEV, False)
     kv = torch.randn(P, 2, Hkv, PS, D, device=DEV).bfloat16()
     q = torch.randn(T, Hq, D, device=DEV).bfloat16()
