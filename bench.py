@@ -39,9 +39,12 @@ def parse():
     ap.add_argument("--model", default="llama3-8b")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--comm", default="fused", choices=["fused", "nccl"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "ttft"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "ttft", "cascade"],
                     help="decode: batched decode throughput (headline); ttft: time to first token with cached "
-                         "chunks vs full prefill (TinyLlama cascade/RAG config)")
+                         "chunks vs full prefill (TinyLlama cascade/RAG config); cascade: shared-context "
+                         "chunk under concurrent queries (Llama-3-70B TP8 config)")
+    ap.add_argument("--ctx-len", type=int, default=8192, help="cascade: shared context chunk tokens")
+    ap.add_argument("--query-len", type=int, default=256, help="cascade: tokens per query")
     return ap.parse_args()
 
 
@@ -50,12 +53,16 @@ class ClockSampler:
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap,timestamp")
 
     def __init__(self, device_index: int):
         self.idx = device_index
         self.proc = None
         self.path = None
+        self.window = None  # (t0, t1) epoch seconds of the timed region; samples outside are dropped
+
+    def mark(self, t0: float, t1: float) -> None:
+        self.window = (t0, t1)
 
     def __enter__(self):
         try:
@@ -79,12 +86,21 @@ class ClockSampler:
     def summary(self) -> dict:
         if not self.path or not os.path.exists(self.path):
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        import datetime
+
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in open(self.path):
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
+            if self.window is not None:
+                try:
+                    ts = datetime.datetime.strptime(parts[9], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                    if not (self.window[0] - 0.1 <= ts <= self.window[1] + 0.1):
+                        continue
+                except ValueError:
+                    pass
             try:
                 sm.append(float(parts[1]))
                 mx = float(parts[2])
@@ -115,6 +131,60 @@ def prompts_for(batch: int, plen: int, vocab: int, seed: int = 3):
     return [torch.randint(3, vocab, (plen,), generator=g).tolist() for _ in range(batch)]
 
 
+def timed_decode(llm, args, n: int):
+    """W untimed then K timed decode steps of every running sequence through
+    ``LLM.step``; returns (device ms = sum of graph-replay events, max over
+    ranks; wall seconds, max over ranks; our kernel launches per step; clocks)."""
+    import torch
+    import torch.distributed as dist
+
+    runner = llm.model_runner
+    # the clock sampler starts before warm-up (nvidia-smi needs ~1 s to start)
+    # and keeps only the samples taken inside the timed region
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        for _ in range(args.warmup):
+            llm.step()
+        # count our kernel launches of one decode step (graph contents)
+        launches = runner.launches_per_decode_step(args.batch)
+        torch.cuda.synchronize()
+        if n > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        runner.event_log = []
+        e0 = time.time()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            llm.step()
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+        clocks.mark(e0, time.time())
+    if n > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    dev_ms = sum(a.elapsed_time(b) for a, b in runner.event_log)
+    runner.event_log = None
+    if len(llm.scheduler.running) != args.batch:
+        raise RuntimeError("batch shrank during the timed region")
+    t = torch.tensor([dev_ms, wall], device="cuda", dtype=torch.float64)
+    if n > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t[0]), float(t[1]), launches, clocks
+
+
+def init_dist(n: int):
+    import torch
+    import torch.distributed as dist
+
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if n > 1 and not dist.is_initialized():
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return rank
+
+
 # --------------------------------------------------------------------- ours
 def run_ours(args) -> None:
     import torch
@@ -125,13 +195,7 @@ def run_ours(args) -> None:
     from braidinfer_b200.ops import _ext
 
     n = args.gpus
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    if n > 1 and not dist.is_initialized():
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+    rank = init_dist(n)
     cfg_dir = make_config_dir(args.model, with_weights=False, rank=rank)
     if n > 1:
         dist.barrier()
@@ -149,32 +213,7 @@ def run_ours(args) -> None:
     while llm.scheduler.waiting:
         llm.step()
     runner = llm.model_runner
-    for _ in range(args.warmup):
-        llm.step()
-    # count our kernel launches of one decode step (graph contents)
-    launches = runner.launches_per_decode_step(args.batch)
-    torch.cuda.synchronize()
-    if n > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    runner.event_log = []
-    with ClockSampler(torch.cuda.current_device()) as clocks:
-        t0 = time.perf_counter()
-        for _ in range(args.steps):
-            llm.step()
-        torch.cuda.synchronize()
-        wall = time.perf_counter() - t0
-    if n > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    dev_ms = sum(a.elapsed_time(b) for a, b in runner.event_log)
-    runner.event_log = None
-    if len(llm.scheduler.running) != args.batch:
-        raise RuntimeError("batch shrank during the timed region")
-    t = torch.tensor([dev_ms, wall], device="cuda", dtype=torch.float64)
-    if n > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    dev_ms, wall = float(t[0]), float(t[1])
+    dev_ms, wall, launches, clocks = timed_decode(llm, args, n)
     toks = args.batch * args.steps
     value = toks / (dev_ms / 1e3)
     e2e = toks / wall
@@ -198,6 +237,78 @@ def run_ours(args) -> None:
             "impl": "ours",
         }
         print(json.dumps(line), flush=True)
+    llm.exit()
+    if n > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ------------------------------------------------------------------ cascade
+def run_cascade(args) -> None:
+    """Shared-context cascade (Llama-3-70B TP8 configuration): one 8192-token
+    context chunk (plus a 32-token system chunk) prefilled once and cascaded
+    under ``batch`` concurrent 256-token queries; reports the decode tok/s of
+    the whole batch and the prefill time of all queries over the cached chunk."""
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, ROOT)
+    from braidinfer_b200 import ChunkedLLM, ChunkType, SamplingParams
+
+    n = args.gpus
+    rank = init_dist(n)
+    model = args.model if args.model != "llama3-8b" else "llama3-70b"
+    cfg_dir = make_config_dir(model, with_weights=False, rank=rank)
+    if n > 1:
+        dist.barrier()
+    B, ctx_len, q_len = args.batch, args.ctx_len, args.query_len
+    page = 256
+    per_seq = q_len + args.warmup + args.steps + 64
+    pages = -(-(32 + ctx_len) // page) + B * -(-per_seq // page) + 16
+    cl = ChunkedLLM(cfg_dir, load_weights=False, tensor_parallel_size=n, max_num_seqs=B,
+                    max_model_len=32 + ctx_len + per_seq, num_kvcache_blocks=pages, kvcache_block_size=page,
+                    max_graph_batch=max(B, 1), comm_backend=args.comm,
+                    max_num_batched_tokens=max(16384, ctx_len + 64, B * q_len))
+    llm = cl.llm
+    vocab = llm.config.spec.vocab_size
+    g = torch.Generator().manual_seed(4)
+    rnd = lambda k: torch.randint(3, vocab, (k,), generator=g).tolist()  # noqa: E731
+    sysc = cl.registry.get(cl.register_chunk("system", ChunkType.SYSTEM_PROMPT, token_ids=rnd(32)))
+    ctx = cl.registry.get(cl.register_chunk("shared context", ChunkType.CONTEXT, token_ids=rnd(ctx_len)))
+    qs = [cl.registry.get(cl.register_chunk(f"query {i}", ChunkType.QUERY, token_ids=rnd(q_len))) for i in range(B)]
+    sp = SamplingParams(temperature=0.0, max_tokens=args.warmup + args.steps + 4, ignore_eos=True)
+    # the shared chunks are prefilled once (first placement), then every query composes over them
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    cl._ensure_kv(cl._place(sysc, [ctx], qs[0]))
+    torch.cuda.synchronize()
+    chunk_ms = (time.perf_counter() - t0) * 1e3
+    for q in qs:
+        cl._ensure_kv(cl._place(sysc, [ctx], q))
+        llm.add_composition({"system_chunk": sysc, "context_chunks": [ctx], "query_chunk": q}, sp)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    while llm.scheduler.waiting:
+        llm.step()
+    torch.cuda.synchronize()
+    first_ms = (time.perf_counter() - t0) * 1e3
+    dev_ms, wall, launches, clocks = timed_decode(llm, args, n)
+    toks = B * args.steps
+    if rank == 0:
+        print(json.dumps({
+            "metric": f"cascade decode tok/s (bs{B}) {model} TP{n}", "value": round(toks / (dev_ms / 1e3), 2),
+            "unit": "tokens/s", "n_gpus": n, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(dev_ms / args.steps, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic token ids (seed 4), random-init weights",
+            "config": {"model": model, "global_batch": B, "shared_context": ctx_len, "query_len": q_len,
+                       "parallelism": f"tp{n}", "comm": args.comm if n > 1 else None},
+            "shared_chunk_prefill_ms": round(chunk_ms, 2),
+            "ttft_all_queries_ms": round(first_ms, 2),
+            "clocks": clocks.summary(),
+            "e2e": {"value": round(toks / wall, 2), "unit": "tokens/s",
+                    "h2d_bytes_per_step": llm.model_runner.last_h2d_bytes, "d2h_bytes_per_step": 4 * B,
+                    "api": "ChunkedLLM chunks + LLM.add_composition + LLM.step"},
+            "gpu_launches": launches * args.steps, "gpu_launches_per_step": launches, "impl": "ours"}), flush=True)
     llm.exit()
     if n > 1:
         dist.barrier()
@@ -342,6 +453,9 @@ def main():
     args = parse()
     if args.impl == "ours" and args.workload == "ttft":
         run_ttft(args)
+        return
+    if args.impl == "ours" and args.workload == "cascade":
+        run_cascade(args)
         return
     if args.impl == "reference":
         run_reference(args)
