@@ -295,7 +295,9 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(const __grid_consta
     fence_barrier_init();
   }
   __syncthreads();
-  pdl_wait();
+  // The step's metadata (plan buffer, page table, RoPE tables) is not written
+  // by the preceding kernel: read it and walk to the first K/V tile before
+  // waiting for that kernel (which produces q and appends this step's K/V).
   pdl_trigger();
   const int t = p.qo_indptr[b];
   if (p.qo_indptr[b + 1] - t < 1) return;
@@ -332,8 +334,11 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(const __grid_consta
     }
   };
   int issued = 0;
+  bool first_v = false;
+  if (warp == 0) first_v = pc_settle(p, pc, r0, r1);
+  pdl_wait();
   if (warp == 0) {
-    bool v = pc_settle(p, pc, r0, r1);
+    bool v = first_v;
     for (; issued < STAGES - 1 && v; ++issued) {
       if (lane == 0) mbar_arrive_expect_tx(&full[issued], 2 * TILE);
       issue(issued);
@@ -496,24 +501,39 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(const __grid_consta
     aw[(warp * 16 + g + 8) * AW_LD + d + 1] = acc[nb][3];
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < G * D; i += 128) {
-    const int row = i / D, d = i % D;
+  // one float4 (4 dims of one head row) per thread and pass
+  for (int i = threadIdx.x; i < G * (D / 4); i += 128) {
+    const int row = i / (D / 4), d = (i % (D / 4)) * 4;
     float M = -INFINITY;
+#pragma unroll
     for (int w = 0; w < 4; ++w) M = fmaxf(M, mw[w * 16 + row]);
-    float L = 0.f, O = 0.f;
+    float L = 0.f;
+    float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
     if (M != -INFINITY) {
+#pragma unroll
       for (int w = 0; w < 4; ++w) {
         const float e = exp2f(mw[w * 16 + row] - M);
         L += lw[w * 16 + row] * e;
-        O += aw[(w * 16 + row) * AW_LD + d] * e;
+        const float* a = aw + (w * 16 + row) * AW_LD + d;
+        O.x += a[0] * e;
+        O.y += a[1] * e;
+        O.z += a[2] * e;
+        O.w += a[3] * e;
       }
     }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    O.x *= inv;
+    O.y *= inv;
+    O.z *= inv;
+    O.w *= inv;
     const int h = kh * G + row;
     if (p.num_splits == 1) {
-      p.out[(size_t)t * p.Hq * D + h * D + d] = f2bf(L > 0.f ? O / L : 0.f);
+      __nv_bfloat16* o = p.out + (size_t)t * p.Hq * D + h * D + d;
+      *reinterpret_cast<__nv_bfloat162*>(o) = __floats2bfloat162_rn(O.x, O.y);
+      *reinterpret_cast<__nv_bfloat162*>(o + 2) = __floats2bfloat162_rn(O.z, O.w);
     } else {
       const size_t idx = ((size_t)t * p.Hq + h) * p.num_splits + split;
-      p.part_o[idx * D + d] = L > 0.f ? O / L : 0.f;
+      *reinterpret_cast<float4*>(p.part_o + idx * D + d) = O;
       if (d == 0) p.part_lse[idx] = L > 0.f ? M + log2f(L) : -INFINITY;
     }
   }
@@ -521,43 +541,51 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(const __grid_consta
   if (p.num_splits == 1) return;
   // ---- the last split CTA of (token, kv head) merges every split's partial
   __shared__ int s_last;
-  __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
     int* c = p.counters + (size_t)t * p.Hkv + kh;
-    const int old = atomicAdd(c, 1);
+    // releases this CTA's partials, acquires the other splits'
+    const int old = atomic_add_acq_rel_gpu(c, 1);
     s_last = old == p.num_splits - 1;
     if (s_last) *c = 0;
   }
   __syncthreads();
   if (!s_last) return;
-  __threadfence();
   const int ns = p.num_splits;
-  for (int i = threadIdx.x; i < G * D; i += 128) {
-    const int row = i / D, d = i % D;
+  for (int i = threadIdx.x; i < G * (D / 4); i += 128) {
+    const int row = i / (D / 4), d = (i % (D / 4)) * 4;
     const size_t base = ((size_t)t * p.Hq + kh * G + row) * ns;
-    float lse[32], o[32];
+    float lse[32];
 #pragma unroll
-    for (int q = 0; q < 32; ++q)
-      if (q < ns) {
-        lse[q] = __ldcg(p.part_lse + base + q);
-        o[q] = __ldcg(p.part_o + (base + q) * D + d);
-      }
+    for (int q = 0; q < 32; ++q) lse[q] = q < ns ? __ldcg(p.part_lse + base + q) : -INFINITY;
     float M = -INFINITY;
 #pragma unroll
-    for (int q = 0; q < 32; ++q)
-      if (q < ns) M = fmaxf(M, lse[q]);
-    float W = 0.f, O = 0.f;
-    if (M != -INFINITY) {
+    for (int q = 0; q < 32; ++q) M = fmaxf(M, lse[q]);
+    float W = 0.f;
+    float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-      for (int q = 0; q < 32; ++q)
-        if (q < ns) {
-          const float w = exp2f(lse[q] - M);
+    for (int q0 = 0; q0 < 32; q0 += 16) {  // at most two passes of 16 partials in flight
+      if (q0 < ns) {
+        float4 o[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k)
+          o[k] = q0 + k < ns ? __ldcg(reinterpret_cast<const float4*>(p.part_o + (base + q0 + k) * D + d))
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          const float w = (M == -INFINITY || q0 + k >= ns) ? 0.f : exp2f(lse[q0 + k] - M);
           W += w;
-          O += w * o[q];
+          O.x += w * o[k].x;
+          O.y += w * o[k].y;
+          O.z += w * o[k].z;
+          O.w += w * o[k].w;
         }
+      }
     }
-    p.out[(size_t)t * p.Hq * D + (kh * G + row) * D + d] = f2bf(W > 0.f ? O / W : 0.f);
+    const float inv = W > 0.f ? 1.f / W : 0.f;
+    __nv_bfloat16* o = p.out + (size_t)t * p.Hq * D + (kh * G + row) * D + d;
+    *reinterpret_cast<__nv_bfloat162*>(o) = __floats2bfloat162_rn(O.x * inv, O.y * inv);
+    *reinterpret_cast<__nv_bfloat162*>(o + 2) = __floats2bfloat162_rn(O.z * inv, O.w * inv);
   }
   if (tr != nullptr && threadIdx.x == 0) tr[5] = globaltimer_ns();
 }
@@ -595,7 +623,7 @@ __global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const __grid_const
     fence_barrier_init();
   }
   __syncthreads();
-  pdl_wait();
+  // metadata first (not written by the preceding kernel), then wait for q / K/V
   pdl_trigger();
   unsigned long long* tr = p.trace
       ? p.trace + 8 * ((size_t)(blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) : nullptr;
@@ -676,8 +704,9 @@ __global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const __grid_const
     }
   };
   int issued = 0;
+  if (warp == 0) settle();
+  pdl_wait();
   if (warp == 0) {
-    settle();
     for (; issued < STAGES - 1 && pc.s < pc.s1; ++issued) {
       if (lane == 0) mbar_arrive_expect_tx(&full[issued], 2 * TILE);
       issue(issued);
