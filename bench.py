@@ -70,7 +70,7 @@ class ClockSampler:
             os.close(fd)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                 "-lms", "50"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
         return self
@@ -90,17 +90,26 @@ class ClockSampler:
 
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        lines = []
         for line in open(self.path):
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 10:
                 continue
-            if self.window is not None:
-                try:
-                    ts = datetime.datetime.strptime(parts[9], "%Y/%m/%d %H:%M:%S.%f").timestamp()
-                    if not (self.window[0] - 0.1 <= ts <= self.window[1] + 0.1):
-                        continue
-                except ValueError:
-                    pass
+            try:
+                ts = datetime.datetime.strptime(parts[9], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+            except ValueError:
+                ts = None
+            lines.append((ts, parts))
+        where = "whole run"
+        if self.window is not None:
+            inside = [x for x in lines if x[0] is not None and self.window[0] <= x[0] <= self.window[1]]
+            where = "timed region"
+            if len(inside) < 2:  # very short timed regions: the samples closest around it
+                mid = 0.5 * (self.window[0] + self.window[1])
+                inside = sorted((x for x in lines if x[0] is not None), key=lambda x: abs(x[0] - mid))[:3]
+                where = "3 samples nearest the timed region"
+            lines = inside
+        for _, parts in lines:
             try:
                 sm.append(float(parts[1]))
                 mx = float(parts[2])
@@ -112,7 +121,7 @@ class ClockSampler:
         os.unlink(self.path)
         sm.sort()
         return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "sampled": where}
 
 
 def make_config_dir(preset: str, with_weights: bool, rank: int = 0) -> str:

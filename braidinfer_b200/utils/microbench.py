@@ -9,6 +9,8 @@
 ``cudaProfilerStart``/``Stop`` (for ``ncu --profile-from-start off``).  Timings
 are taken after warm-up with CUDA events on the launching stream; ``--graph``
 replays 20 back-to-back launches from a CUDA graph (the decode setting).
+Consecutive launches rotate through enough copies of the weights / KV pool /
+activations to exceed twice the 126 MB L2, so every launch reads from HBM.
 """
 from __future__ import annotations
 
@@ -18,19 +20,29 @@ import math
 import torch
 
 
+L2_BYTES = 126 << 20
+
+
+def _copies(nbytes: int) -> int:
+    """Input copies whose total exceeds twice the L2, so that consecutive
+    launches (which rotate through them) read from HBM, not from L2."""
+    return max(2, min(64, -(-2 * L2_BYTES // max(1, nbytes)) + 1))
+
+
 def _graph_time(fn, n: int = 20) -> float:
-    for _ in range(3):
-        fn()
+    """fn(i) launches with input copy i; n launches replayed from one graph."""
+    for i in range(3):
+        fn(i)
     torch.cuda.synchronize()
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):
-        fn()
+        fn(0)
     torch.cuda.current_stream().wait_stream(s)
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
-        for _ in range(n):
-            fn()
+        for i in range(n):
+            fn(i)
     g.replay()
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -42,13 +54,13 @@ def _graph_time(fn, n: int = 20) -> float:
 
 
 def _eager_time(fn, n: int = 10) -> float:
-    for _ in range(3):
-        fn()
+    for i in range(3):
+        fn(i)
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
-    for _ in range(n):
-        fn()
+    for i in range(n):
+        fn(i)
     b.record()
     torch.cuda.synchronize()
     return a.elapsed_time(b) / n * 1e3
@@ -58,16 +70,18 @@ def bench_gemm(M: int, N: int, K: int, epi: int = 0, graph: bool = False, splits
                rms: bool = False) -> dict:
     from ..ops._ext import ext
 
-    x = torch.randn(M, K, device="cuda").bfloat16()
-    w = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
+    nc = _copies((N + M) * K * 2)  # weight and activation copies rotate: HBM, not L2
+    xs = [torch.randn(M, K, device="cuda").bfloat16() for _ in range(nc)]
+    w0 = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
+    ws = [w0] + [w0.clone() for _ in range(nc - 1)]
     out = torch.empty(M, N // 2 if epi else N, device="cuda", dtype=torch.bfloat16)
     ext().gemm_force_splits(splits)
-    fn = lambda: ext().gemm(out, x, w, None, None, epi, 1e-5 if rms else -1.0)  # noqa: E731
+    fn = lambda i: ext().gemm(out, xs[i % nc], ws[i % nc], None, None, epi, 1e-5 if rms else -1.0)  # noqa: E731
     us = (_graph_time if graph else _eager_time)(fn)
     ext().gemm_force_splits(-1)
     return {"kernel": "gemm_tcgen05", "M": M, "N": N, "K": K, "epi": epi, "rms": rms, "splits": splits,
             "us": round(us, 2), "weight_TBps": round(N * K * 2 / us / 1e6, 3),
-            "TFLOPS": round(2 * M * N * K / us / 1e6, 1)}
+            "TFLOPS": round(2 * M * N * K / us / 1e6, 1), "l2": f"{nc} rotating input copies (> L2)"}
 
 
 def _decode_meta(B: int, L: int, PS: int = 256):
@@ -85,15 +99,16 @@ def bench_attn_decode(B: int, L: int, Hq: int, Hkv: int, splits: int = 0, D: int
     from .. import ops
 
     meta, npg = _decode_meta(B, L)
-    kv = torch.randn(B * npg + 1, 2, Hkv, 256, D, device="cuda").bfloat16()
+    byts = B * L * Hkv * D * 2 * 2
+    nc = _copies(byts)
+    kvs = [torch.randn(B * npg + 1, 2, Hkv, 256, D, device="cuda").bfloat16() for _ in range(nc)]
     q = torch.randn(B, Hq, D, device="cuda").bfloat16()
     cos, sin = ops.build_cos_sin(D, 500000.0, 2 * L + 16, device="cuda")
     sms = torch.cuda.get_device_properties(0).multi_processor_count
-    meta.num_splits = splits or max(1, min(32, (2 * sms) // (B * Hkv)))
-    us = _graph_time(lambda: ops.attention(q, kv, meta, cos, sin, D ** -0.5))
-    byts = B * L * Hkv * D * 2 * 2
+    meta.num_splits = splits or max(1, min(32, -(-(2 * sms) // (B * Hkv)), -(-L // 64)))
+    us = _graph_time(lambda i: ops.attention(q, kvs[i % nc], meta, cos, sin, D ** -0.5))
     return {"kernel": "attn_decode", "B": B, "L": L, "Hq": Hq, "Hkv": Hkv, "splits": meta.num_splits,
-            "us": round(us, 2), "kv_TBps": round(byts / us / 1e6, 3)}
+            "us": round(us, 2), "kv_TBps": round(byts / us / 1e6, 3), "l2": f"{nc} rotating KV pools (> L2)"}
 
 
 def bench_attn_prefill(L: int, Hq: int, Hkv: int, B: int = 1, D: int = 128, ctx: int = 0,
@@ -118,10 +133,13 @@ def bench_attn_prefill(L: int, Hq: int, Hkv: int, B: int = 1, D: int = 128, ctx:
                     seg_offset=i32(soff), seg_len=i32(slen), seg_pos0=i32(spos0), seg_delta=i32([0] * len(slen)),
                     page_ids=i32(list(range(B * per))), num_seqs=B, max_q_len=L, max_kv_len=L + ctx, decode=False,
                     num_splits=splits or 1)
-    kv = torch.randn(B * per + 1, 2, Hkv, PS, D, device="cuda").bfloat16()
-    q = torch.randn(B * L, Hq, D, device="cuda").bfloat16()
+    kv_bytes = (B * per + 1) * 2 * Hkv * PS * D * 2
+    nc = _copies(kv_bytes + B * L * Hq * D * 2)
+    kvs = [torch.randn(B * per + 1, 2, Hkv, PS, D, device="cuda").bfloat16() for _ in range(nc)]
+    qs = [torch.randn(B * L, Hq, D, device="cuda").bfloat16() for _ in range(nc)]
     cos, sin = ops.build_cos_sin(D, 500000.0, 2 * (L + ctx) + 16, device="cuda")
-    us = (_graph_time if graph else _eager_time)(lambda: ops.attention(q, kv, meta, cos, sin, D ** -0.5))
+    us = (_graph_time if graph else _eager_time)(
+        lambda i: ops.attention(qs[i % nc], kvs[i % nc], meta, cos, sin, D ** -0.5))
     flops = B * 4 * (L * L / 2 + L * ctx) * Hq * D
     return {"kernel": "attn_prefill", "L": L, "ctx": ctx, "Hq": Hq, "Hkv": Hkv, "D": D, "B": B, "us": round(us, 1),
             "TFLOPS_causal": round(flops / us / 1e6, 1)}

@@ -62,6 +62,7 @@ struct AttnParams {
   float* part_lse;  // [T, Hq, splits]
   int* counters;    // [T * Hkv] split arrival counters, kept at zero between launches
   unsigned long long* trace;  // optional per-CTA phase timestamps (profiling)
+  unsigned long long* span;   // optional launch span (profiling)
 };
 
 constexpr float LOG2E = 1.4426950408889634f;
@@ -287,6 +288,7 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(const __grid_consta
       ? p.trace + 8 * ((size_t)(blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) : nullptr;
   if (threadIdx.x == 0) {
     if (tr != nullptr) tr[0] = globaltimer_ns();
+    span_start(p.span);
     tma_prefetch_desc(&tmkv);
     for (int i = 0; i < STAGES; ++i) {
       mbar_init(&full[i], 1);
@@ -337,6 +339,7 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(const __grid_consta
   bool first_v = false;
   if (warp == 0) first_v = pc_settle(p, pc, r0, r1);
   pdl_wait();
+  if (threadIdx.x == 0) span_waited(p.span);
   if (warp == 0) {
     bool v = first_v;
     for (; issued < STAGES - 1 && v; ++issued) {
@@ -538,7 +541,10 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(const __grid_consta
     }
   }
   if (tr != nullptr && threadIdx.x == 0) tr[4] = globaltimer_ns();
-  if (p.num_splits == 1) return;
+  if (p.num_splits == 1) {
+    if (threadIdx.x == 0) span_end(p.span);
+    return;
+  }
   // ---- the last split CTA of (token, kv head) merges every split's partial
   __shared__ int s_last;
   __syncthreads();
@@ -550,7 +556,10 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(const __grid_consta
     if (s_last) *c = 0;
   }
   __syncthreads();
-  if (!s_last) return;
+  if (!s_last) {
+    if (threadIdx.x == 0) span_end(p.span);
+    return;
+  }
   const int ns = p.num_splits;
   for (int i = threadIdx.x; i < G * (D / 4); i += 128) {
     const int row = i / (D / 4), d = (i % (D / 4)) * 4;
@@ -588,6 +597,7 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(const __grid_consta
     *reinterpret_cast<__nv_bfloat162*>(o + 2) = __floats2bfloat162_rn(O.z * inv, O.w * inv);
   }
   if (tr != nullptr && threadIdx.x == 0) tr[5] = globaltimer_ns();
+  if (threadIdx.x == 0) span_end(p.span);
 }
 
 // -------------------------------------------------------------- prefill
@@ -615,6 +625,7 @@ __global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const __grid_const
   const int b = blockIdx.y, kh = blockIdx.z / S, split = blockIdx.z % S;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
+    span_start(p.span);
     tma_prefetch_desc(&tmkv);
     for (int i = 0; i < STAGES; ++i) {
       mbar_init(&full[i], 1);
@@ -706,6 +717,7 @@ __global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const __grid_const
   int issued = 0;
   if (warp == 0) settle();
   pdl_wait();
+  if (threadIdx.x == 0) span_waited(p.span);
   if (warp == 0) {
     for (; issued < STAGES - 1 && pc.s < pc.s1; ++issued) {
       if (lane == 0) mbar_arrive_expect_tx(&full[issued], 2 * TILE);
@@ -877,6 +889,7 @@ __global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const __grid_const
             __floats2bfloat162_rn(acc[nb][2 * h] * inv, acc[nb][2 * h + 1] * inv);
       }
     }
+    if (threadIdx.x == 0) span_end(p.span);
     return;
   }
   // ---- split: publish this CTA's partial, the last CTA of the q tile merges
@@ -903,7 +916,10 @@ __global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const __grid_const
   }
   __syncthreads();
   if (tr != nullptr && threadIdx.x == 0) tr[3] = globaltimer_ns();
-  if (!s_last) return;
+  if (!s_last) {
+    if (threadIdx.x == 0) span_end(p.span);
+    return;
+  }
   // merge weights per row in shared memory (the K ring is idle now); every
   // lse / partial load of a row is issued before any is used
   float* wsm = reinterpret_cast<float*>(kbuf);  // [64][S]
@@ -974,6 +990,7 @@ __global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const __grid_const
     }
   }
   if (tr != nullptr && threadIdx.x == 0) tr[4] = globaltimer_ns();
+  if (threadIdx.x == 0) span_end(p.span);
 }
 
 // ------------------------------------------------------------------ host
@@ -984,6 +1001,7 @@ void attn_set_trace(torch::Tensor buf) {
 }
 
 int gemm_num_sms();
+unsigned long long* next_span();
 
 // Per-device split-merge counters (zeroed once; the merging CTA re-arms its counter).
 static int* attn_counters(int dev, size_t n) {
@@ -1116,6 +1134,7 @@ void attention(torch::Tensor out, torch::Tensor q, torch::Tensor kv, torch::Tens
     n_counters = (size_t)qt * num_seqs * Hkv;
   }
   p.trace = g_attn_trace;
+  p.span = next_span();
   torch::Tensor po, pl;
   if (p.num_splits > 1) {
     if (part_o.has_value() && part_o->defined() && part_o->numel() >= (int64_t)T * Hq * p.num_splits * D) {

@@ -61,6 +61,18 @@ BRAID_DEVICE uint64_t globaltimer_ns() {
   return t;
 }
 
+// Launch-span trace (profiling): span[0] = earliest CTA start, span[1] =
+// earliest time a CTA passed its dependency wait, span[2] = latest CTA end.
+BRAID_DEVICE void span_start(unsigned long long* span) {
+  if (span != nullptr) atomicMin(span, (unsigned long long)globaltimer_ns());
+}
+BRAID_DEVICE void span_waited(unsigned long long* span) {
+  if (span != nullptr) atomicMin(span + 1, (unsigned long long)globaltimer_ns());
+}
+BRAID_DEVICE void span_end(unsigned long long* span) {
+  if (span != nullptr) atomicMax(span + 2, (unsigned long long)globaltimer_ns());
+}
+
 // Acquire load at system scope (flags written by peer GPUs over NVLink).
 BRAID_DEVICE uint64_t ld_acquire_sys_u64(const uint64_t* p) {
   uint64_t v;

@@ -81,10 +81,12 @@ __global__ void __launch_bounds__(192, 1) gemm_persistent_kernel(const __grid_co
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
   pdl_trigger();
+  if (threadIdx.x == 0) span_start(args.span);
 
   if (warp == 0) {
     if (lane == 0) {
       pdl_wait();
+      span_waited(args.span);
       uint32_t g = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
@@ -179,6 +181,7 @@ __global__ void __launch_bounds__(192, 1) gemm_persistent_kernel(const __grid_co
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
   }
+  if (threadIdx.x == 0) span_end(args.span);
 }
 
 template <int BN, int STAGES>

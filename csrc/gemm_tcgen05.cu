@@ -125,6 +125,7 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
   unsigned long long* tr = args.trace
       ? args.trace + 8 * ((size_t)(blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) : nullptr;
   if (tr != nullptr && threadIdx.x == 0) tr[0] = globaltimer_ns();
+  if (threadIdx.x == 0) span_start(args.span);
 
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
@@ -165,6 +166,7 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
         tma_load_2d(ringA + i * S::A_BYTES, &tmA, &full[i], (kb0 + i) * BK, m0);
       }
       pdl_wait();
+      span_waited(args.span);
       // sequence-parallel prefill: the A rows must have been gathered from their owners
       if (!args.swap && !sp_wait_rows(args.sp, m0, min(m0 + BM, args.M))) atomicExch(args.err, 4);
       for (int i = 0; i < pre; ++i) tma_load_2d(ringB + i * S::B_BYTES, &tmB, &full[i], (kb0 + i) * BK, n0);
@@ -488,6 +490,7 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
   }
+  if (threadIdx.x == 0) span_end(args.span);
 }
 
 // ------------------------------------------------------------------ host side
@@ -605,6 +608,23 @@ int gemm_num_sms() {
   return n;
 }
 
+static unsigned long long* g_span_buf = nullptr;
+static int64_t g_span_cap = 0, g_span_seq = 0;
+// Profiling: record the span of every later GEMM / attention launch into
+// consecutive 4 x u64 slots of `buf` (an empty tensor switches it off).
+// Returns the number of slots used since the previous call.
+int64_t span_trace(torch::Tensor buf) {
+  const int64_t used = g_span_seq;
+  g_span_buf = buf.defined() && buf.numel() ? reinterpret_cast<unsigned long long*>(buf.data_ptr<int64_t>()) : nullptr;
+  g_span_cap = g_span_buf ? buf.numel() / 4 : 0;
+  g_span_seq = 0;
+  return used;
+}
+unsigned long long* next_span() {
+  if (g_span_buf == nullptr || g_span_seq >= g_span_cap) return nullptr;
+  return g_span_buf + 4 * (g_span_seq++);
+}
+
 static int g_forced_splits = -1;
 // Tuning: force the split-K factor of later tile-per-CTA launches (0 = heuristic, -1 = environment).
 void gemm_force_splits(int64_t n) { g_forced_splits = (int)n; }
@@ -705,6 +725,7 @@ static int64_t run_gemm(GemmArgs& a, const torch::Tensor& x, const torch::Tensor
     a.err = scratch_for(x.get_device(), 0, 0).err;
     CUtensorMap ta = make_tmap(x.data_ptr(), T, K, x.stride(0), BM);
     CUtensorMap tb = make_tmap(w.data_ptr(), F, K, w.stride(0), BN);
+    a.span = next_span();
     launch_gemm_persistent(ta, tb, a, BN, st);
     return arrivals;
   }
@@ -751,6 +772,7 @@ static int64_t run_gemm(GemmArgs& a, const torch::Tensor& x, const torch::Tensor
   a.counters = sc.counters;
   a.err = sc.err;
   a.trace = g_trace;
+  a.span = next_span();
   dim3 grid(m_tiles, n_tiles, splits);
   const void* pa = swap ? w.data_ptr() : x.data_ptr();
   const void* pb = swap ? x.data_ptr() : w.data_ptr();

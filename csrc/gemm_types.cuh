@@ -83,6 +83,7 @@ struct GemmArgs {
   PushEpi push;
   SpArgs sp;
   unsigned long long* trace;  // optional per-CTA phase timestamps (profiling)
+  unsigned long long* span;   // optional launch span (profiling)
 };
 
 constexpr int BM = 128;
@@ -296,5 +297,7 @@ BRAID_DEVICE void store_tile_normal(const GemmArgs& args, int m0, int n0, int r,
 void launch_gemm_persistent(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int BN,
                             cudaStream_t st);
 int gemm_num_sms();
+// Profiling: the next launch's span slot (4 x u64) when span tracing is on, else nullptr.
+unsigned long long* next_span();
 
 }  // namespace braid
