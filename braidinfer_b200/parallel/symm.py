@@ -67,6 +67,10 @@ class FusedComm:
         data = 2 * tp.size * max_tokens * hidden * 2
         self.flags_off = align(data)
         off = self.flags_off + align(8 * tp.size)
+        # per-(source, 128-feature tile) flags of the in-GEMM all-reduce
+        self.max_tiles = -(-hidden // 128)
+        self.tile_flags_off = off
+        off += align(8 * tp.size * self.max_tiles)
         # sequence-parallel prefill region
         self.sp_max = sp_max_tokens if sp_max_tokens > max_tokens else 0
         self.rs_flags_off = off
@@ -100,6 +104,8 @@ class FusedComm:
         self.epoch_state = torch.zeros(4, dtype=torch.int64, device=device)
         self.status = torch.zeros(4, dtype=torch.int32, device=device)
         self.push_fault = False  # test hook: skip the push (a peer that never signals)
+        import os
+        self.fused_reduce = os.environ.get("BRAID_TP_FUSED_REDUCE", "0") == "1"
         dist.barrier(group=tp.group)
         log.info("fused comm ready: tp=%d maxT=%d hidden=%d (%.1f MB buffer)", tp.size, max_tokens, hidden,
                  nbytes / 1e6)
@@ -182,7 +188,16 @@ class FusedComm:
         return self._reduce(residual, residual, self._push_arrivals(partial))
 
     def linear_all_reduce_add(self, x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor) -> torch.Tensor:
-        """``residual += sum_ranks(x @ w.T)`` with the push fused into the GEMM epilogue."""
+        """``residual += sum_ranks(x @ w.T)`` in ONE kernel: each 128-feature tile
+        is pushed to every peer from the GEMM epilogue, the tile's CTA waits for
+        the peers' copies of the same tile and reduces them with the residual.
+        ``fused_reduce = False`` keeps the two-kernel form (push epilogue, then
+        ``tp_reduce_add``)."""
+        if self.fused_reduce and residual.is_contiguous() and self.tp.size <= 8:
+            self._C.gemm_allreduce_add(residual, x, w, self.peers, self.flags_off, self.tile_flags_off,
+                                       self.max_tiles, self.tp.rank, self.tp.size, self.maxT, self.epoch_state,
+                                       self.status, self.timeout_s)
+            return residual
         arrivals = self._C.gemm_push(x, w, self.peers, self.flags_off, self.tp.rank, self.tp.size, self.maxT,
                                      self.epoch_state)
         return self._reduce(residual, residual, arrivals)

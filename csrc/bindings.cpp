@@ -21,6 +21,9 @@ int64_t gemm_check_error(int64_t device);
 void gemm_set_trace(torch::Tensor buf);
 void gemm_force_splits(int64_t n);
 int64_t span_trace(torch::Tensor buf);
+void gemm_allreduce_add(torch::Tensor residual, torch::Tensor x, torch::Tensor w, torch::Tensor peers,
+                        int64_t flags_off, int64_t tile_flags_off, int64_t max_tiles, int64_t rank, int64_t tp,
+                        int64_t maxT, torch::Tensor epoch_state, torch::Tensor status, double timeout_s);
 int64_t gemm_push(torch::Tensor x, torch::Tensor w, torch::Tensor peers, int64_t flags_off, int64_t rank, int64_t tp,
                   int64_t maxT, torch::Tensor epoch_state);
 std::vector<torch::Tensor> comm_alloc(int64_t nbytes, int64_t device);
@@ -67,6 +70,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "sequence-parallel reduce of pushed partial rows + all-gather of the new rows and their 1/rms");
   m.def("sp_wait", &braid::sp_wait, "bounded wait for every owner's all-gather");
   m.def("comm_tensor", &braid::comm_tensor, "tensor view of comm-buffer memory");
+  m.def("gemm_allreduce_add", &braid::gemm_allreduce_add,
+        "row-parallel GEMM with the TP all-reduce (+ residual) done inside the kernel over peer memory");
   m.def("gemm_push", &braid::gemm_push, "row-parallel GEMM whose epilogue pushes bf16 tiles to TP peers");
   m.def("comm_alloc", &braid::comm_alloc, "cudaMalloc a comm buffer; returns (ptr, ipc handle)");
   m.def("comm_open", &braid::comm_open, "map a peer's comm buffer from its IPC handle");

@@ -80,6 +80,11 @@ BRAID_DEVICE uint64_t ld_acquire_sys_u64(const uint64_t* p) {
   return v;
 }
 
+// Release store at system scope (a flag a peer GPU polls).
+BRAID_DEVICE void st_release_sys_u64(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" :: "l"(p), "l"(v) : "memory");
+}
+
 // Orders this thread's earlier generic-proxy accesses (and what they acquired)
 // before its later async-proxy (TMA) accesses of global memory.
 BRAID_DEVICE void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }

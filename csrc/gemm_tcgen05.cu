@@ -415,10 +415,82 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
         }
         __threadfence_system();
         named_bar_sync(1, 128);
-        if (et == 0) {
-          for (int p = 0; p < ps.tp; ++p)
-            atomicAdd(reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(ps.peers[p]) + ps.flags_off) +
-                          ps.rank, 1ull);
+        if (!ps.fused) {
+          if (et == 0) {
+            for (int p = 0; p < ps.tp; ++p)
+              atomicAdd(reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(ps.peers[p]) + ps.flags_off) +
+                            ps.rank, 1ull);
+          }
+        } else {
+          // fused all-reduce of this 128-feature tile
+          const uint64_t epoch = ps.epoch_state[0];
+          if (et == 0) {
+            __threadfence_system();
+            for (int p = 0; p < ps.tp; ++p)
+              st_release_sys_u64(reinterpret_cast<uint64_t*>(reinterpret_cast<char*>(ps.peers[p]) + ps.tile_flags_off) +
+                                     (size_t)ps.rank * ps.max_tiles + m_tile,
+                                 epoch + 1);
+          }
+          int* s_ok = s_flag;
+          if (et == 0) *s_ok = 1;
+          named_bar_sync(1, 128);
+          if (et < ps.tp) {
+            const uint64_t* f = reinterpret_cast<const uint64_t*>(reinterpret_cast<const char*>(ps.peers[ps.rank]) +
+                                                                  ps.tile_flags_off) + (size_t)et * ps.max_tiles + m_tile;
+            const uint64_t t0 = globaltimer_ns();
+            while (ld_acquire_sys_u64(f) < epoch + 1) {
+              if (globaltimer_ns() - t0 > ps.timeout_ns) {
+                if (atomicCAS(ps.status, 0, 1) == 0) {
+                  ps.status[1] = ps.rank;
+                  ps.status[2] = et;
+                  ps.status[3] = (int)epoch;
+                }
+                *s_ok = 0;
+                break;
+              }
+              __nanosleep(32);
+            }
+          }
+          named_bar_sync(1, 128);
+          if (*s_ok && m < args.M) {
+            // 8 tokens x up to 8 sources of this feature per pass, all loads in flight
+            const __nv_bfloat16* recv = reinterpret_cast<const __nv_bfloat16*>(ps.peers[ps.rank]) +
+                                        (size_t)slot * ps.tp * ps.maxT * args.M + m;
+            for (int t0 = 0; t0 < args.N; t0 += 8) {
+              __nv_bfloat16 pv[8][8];
+              float res[8];
+#pragma unroll
+              for (int src = 0; src < 8; ++src)
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                  pv[src][j] = (src < ps.tp && t0 + j < args.N)
+                                   ? __ldcv(recv + ((size_t)src * ps.maxT + t0 + j) * args.M)
+                                   : __float2bfloat16(0.f);
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                res[j] = (args.residual && t0 + j < args.N) ? bf2f(args.residual[(size_t)(t0 + j) * args.ldr + m])
+                                                            : 0.f;
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                if (t0 + j >= args.N) continue;
+                float acc = 0.f;
+#pragma unroll
+                for (int src = 0; src < 8; ++src) acc += bf2f(pv[src][j]);
+                args.out[(size_t)(t0 + j) * args.ldo + m] = f2bf(res[j] + rbf(acc));
+              }
+            }
+          }
+          // the last tile to finish advances the epoch
+          named_bar_sync(1, 128);
+          if (et == 0) {
+            __threadfence();
+            const unsigned long long done =
+                atomicAdd(reinterpret_cast<unsigned long long*>(ps.epoch_state + 2), 1ull);
+            if (done == (unsigned long long)(gridDim.x * gridDim.y - 1)) {
+              ps.epoch_state[2] = 0;
+              ps.epoch_state[0] = epoch + 1;
+            }
+          }
         }
       } else if (args.epi == 1) {
         // Swapped SwiGLU: tile rows [0,64) gate, [64,128) up of the same 64 features.
@@ -868,6 +940,34 @@ namespace braid {
 // Row-parallel GEMM whose epilogue pushes the result to every tensor-parallel
 // peer (decode shapes).  Returns the number of tiles pushed, i.e. the arrivals
 // each peer must count from this rank for this call.
+// residual += sum over the TP group of x @ w^T, reduced inside this GEMM (see PushEpi).
+void gemm_allreduce_add(torch::Tensor residual, torch::Tensor x, torch::Tensor w, torch::Tensor peers,
+                        int64_t flags_off, int64_t tile_flags_off, int64_t max_tiles, int64_t rank, int64_t tp,
+                        int64_t maxT, torch::Tensor epoch_state, torch::Tensor status, double timeout_s) {
+  TORCH_CHECK(x.size(0) <= 64 && x.size(0) <= maxT, "gemm_allreduce_add: decode shapes only (<= 64 tokens)");
+  TORCH_CHECK(w.size(0) <= max_tiles * BM, "gemm_allreduce_add: too many output tiles for the flag area");
+  TORCH_CHECK(tp >= 1 && tp <= 8, "gemm_allreduce_add: one NVLink domain of at most 8 ranks");
+  TORCH_CHECK(residual.is_contiguous() && residual.size(0) == x.size(0) && residual.size(1) == w.size(0));
+  GemmArgs a{};
+  a.epi = 3;
+  a.out = reinterpret_cast<__nv_bfloat16*>(residual.data_ptr());
+  a.ldo = residual.stride(0);
+  a.residual = a.out;
+  a.ldr = a.ldo;
+  a.push.peers = reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>());
+  a.push.flags_off = flags_off;
+  a.push.epoch_state = reinterpret_cast<uint64_t*>(epoch_state.data_ptr<int64_t>());
+  a.push.rank = rank;
+  a.push.tp = tp;
+  a.push.maxT = maxT;
+  a.push.fused = 1;
+  a.push.tile_flags_off = tile_flags_off;
+  a.push.max_tiles = (int)max_tiles;
+  a.push.status = status.data_ptr<int>();
+  a.push.timeout_ns = (uint64_t)(timeout_s * 1e9);
+  run_gemm(a, x, w, false);
+}
+
 int64_t gemm_push(torch::Tensor x, torch::Tensor w, torch::Tensor peers, int64_t flags_off, int64_t rank, int64_t tp,
                   int64_t maxT, torch::Tensor epoch_state) {
   TORCH_CHECK(x.size(0) <= 64 && x.size(0) <= maxT, "gemm_push: decode shapes only (<= 64 tokens)");
@@ -875,7 +975,7 @@ int64_t gemm_push(torch::Tensor x, torch::Tensor w, torch::Tensor peers, int64_t
   a.epi = 3;
   a.push.peers = reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>());
   a.push.flags_off = flags_off;
-  a.push.epoch_state = reinterpret_cast<const uint64_t*>(epoch_state.data_ptr<int64_t>());
+  a.push.epoch_state = reinterpret_cast<uint64_t*>(epoch_state.data_ptr<int64_t>());
   a.push.rank = rank;
   a.push.tp = tp;
   a.push.maxT = maxT;

@@ -29,11 +29,25 @@ struct QkvEpi {
 // every tensor-parallel peer's receive area (slot epoch & 1, source row rank)
 // instead of local memory, then each peer's arrival counter for this rank is
 // bumped; tp_reduce_add in comm.cu completes the all-reduce.
+//
+// Fused all-reduce (fused == 1): the same push, then per 128-feature tile a
+// release flag (value epoch + 1) in every peer's tile_flags[rank][tile]; the
+// tile's CTA waits (bounded) until every source's flag for this tile reached
+// epoch + 1, sums the tp received tiles in fp32, adds the residual and writes
+// the result in place.  The last tile to finish advances the epoch
+// (epoch_state[2] counts finished tiles).  All CTAs of the grid are resident
+// at once (the split factor keeps the grid within one wave), so the per-tile
+// waits cannot block a CTA that has not started.
 struct PushEpi {
   const uint64_t* peers;       // [tp] base addresses of the peers' comm buffers
   int64_t flags_off;           // byte offset of the arrival counters in a comm buffer
-  const uint64_t* epoch_state; // local epoch (completed all-reduce calls)
+  uint64_t* epoch_state;       // local [0] epoch (completed all-reduce calls), [2] finished tiles
   int rank, tp, maxT;
+  int fused;                   // 1: wait for the peers' tiles and reduce in this kernel
+  int64_t tile_flags_off;      // byte offset of u64 tile_flags[tp][max_tiles]
+  int max_tiles;
+  int* status;                 // comm status word {code, rank, peer, epoch}
+  uint64_t timeout_ns;
 };
 
 // Sequence-parallel tensor parallelism for prefill-sized batches.  Token rows

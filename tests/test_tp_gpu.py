@@ -58,17 +58,22 @@ def _w_allreduce(rank, world, port, q):
             torch.cuda.synchronize()
             fc.check()
             errs.append((out.float() - ref).abs().max().item())
-        # GEMM with the push fused into its epilogue
-        xw = torch.randn(5, 512, device="cuda").bfloat16()
+        # GEMM with the all-reduce inside the kernel (fused_reduce) and, in
+        # between, the two-kernel form (push epilogue + reduce kernel)
         w = (torch.randn(1024, 512, device="cuda", generator=torch.Generator(device="cuda").manual_seed(rank)) * 0.05).bfloat16()
-        part = (xw.float() @ w.float().t()).bfloat16()
-        ref = part.float().clone()
-        dist.all_reduce(ref)
-        res = torch.zeros(5, 1024, device="cuda", dtype=torch.bfloat16)
-        out = fc.linear_all_reduce_add(xw, w, res)
-        torch.cuda.synchronize()
-        fc.check()
-        errs.append((out.float() - ref).abs().max().item())
+        for it, (T, fused) in enumerate([(5, True), (1, True), (16, False), (8, True), (13, True), (3, False),
+                                         (16, True)]):
+            xw = torch.randn(T, 512, device="cuda", generator=torch.Generator(device="cuda").manual_seed(50 + it + 7 * rank)).bfloat16()
+            part = (xw.float() @ w.float().t()).bfloat16()
+            ref = part.float().clone()
+            dist.all_reduce(ref)
+            res0 = torch.randn(T, 1024, device="cuda", generator=torch.Generator(device="cuda").manual_seed(90 + it)).bfloat16()
+            ref = res0.float() + ref.bfloat16().float()
+            fc.fused_reduce = fused
+            out = fc.linear_all_reduce_add(xw, w, res0.clone())
+            torch.cuda.synchronize()
+            fc.check()
+            errs.append((out.float() - ref).abs().max().item())
         q.put((rank, errs))
         fc.close()
     except Exception:
