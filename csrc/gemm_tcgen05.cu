@@ -528,7 +528,8 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
 #pragma unroll
           for (int j = 0; j < 16; ++j) xch[r * XCH_LD + j] = rbf(v[j]);
           named_bar_sync(1, 128);
-          for (int j = ew; j < 16; j += 4) {
+#pragma unroll
+          for (int j = ew; j < 16; j += 4) {  // unrolled: the tokens' metadata loads overlap
             const int t = n0 + c0 + j;
             if (t >= args.N) continue;
             for (int hl = 0; hl < BM / D; ++hl) {
