@@ -4,6 +4,7 @@
     python -m braidinfer_b200.utils.microbench attn-decode B L HQ HKV [--splits S]
     python -m braidinfer_b200.utils.microbench attn-prefill L HQ HKV [--batch B] [--ctx C] [--head-dim D] [--splits S]
     python -m braidinfer_b200.utils.microbench decode-step MODEL B PROMPT_LEN
+    torchrun --nproc-per-node N -m braidinfer_b200.utils.microbench tp-gemm [--tokens-decode 8] ...
 
 ``decode-step`` runs one eager decode step of a random-init model between
 ``cudaProfilerStart``/``Stop`` (for ``ncu --profile-from-start off``).  Timings
@@ -174,6 +175,96 @@ def decode_step(model: str, B: int, plen: int) -> None:
     torch.cuda.cudart().cudaProfilerStop()
 
 
+def bench_tp_gemm(T_dec: int = 8, T_pre: int = 4096, H: int = 4096, I: int = 14336) -> None:
+    """Row-parallel GEMM + its collective over the TP group (run under torchrun,
+    one process per GPU).  Llama-3-8B down_proj shape: ``x [T, I/tp] @ w[H, I/tp]^T``.
+
+    * decode (T_dec tokens): our GEMM whose epilogue pushes tiles to every peer
+      + bounded-wait reduce kernel, vs ``F.linear``-equivalent GEMM + NCCL
+      all_reduce; both replayed from CUDA graphs.
+    * prefill (T_pre tokens): our GEMM with the reduce-scatter epilogue + owner
+      reduce / all-gather of rows and 1/rms (sequence parallel), vs GEMM + NCCL
+      all_reduce; eager.
+    Times are device time (CUDA events), max over ranks.  Roofline per GPU = the
+    slower of the GEMM at the bf16 peak, its weight bytes at HBM bandwidth and
+    the bytes it must send over NVLink at the measured 770 GB/s per direction.
+    """
+    import datetime
+    import json
+    import os
+
+    import torch.distributed as dist
+
+    from .. import ops
+    from ..ops._ext import ext
+    from ..parallel.state import init_tp
+    from ..parallel.symm import FusedComm
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    tp = init_tp(dist.get_world_size())
+    n, rank = tp.size, tp.rank
+    K = I // n
+    fc = FusedComm(tp, H, torch.device("cuda", local), max_tokens=64, timeout_s=10.0, sp_max_tokens=T_pre)
+    PEAK, HBM, LINK = 1.59e15, 6.65e12, 770e9
+    nw = _copies(H * K * 2)
+    ws = [(torch.randn(H, K, device="cuda") * 0.02).bfloat16() for _ in range(nw)]
+
+    def maxrank(us: float) -> float:
+        t = torch.tensor([us], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    out = {"kernel": "tp_gemm_collective", "tp": n, "H": H, "K_per_rank": K}
+    # ---- decode: one-shot push all-reduce (graph) vs NCCL all_reduce (graph)
+    x = torch.randn(T_dec, K, device="cuda").bfloat16()
+    res = torch.zeros(T_dec, H, device="cuda", dtype=torch.bfloat16)
+    y = torch.empty(T_dec, H, device="cuda", dtype=torch.bfloat16)
+    ours = maxrank(_graph_time(lambda i: fc.linear_all_reduce_add(x, ws[i % nw], res)))
+    fc.check()
+
+    def nccl_dec(i):
+        ext().gemm(y, x, ws[i % nw], None, None, 0, -1.0)
+        dist.all_reduce(y, group=tp.group)
+
+    base = maxrank(_graph_time(nccl_dec))
+    roof = max(2 * T_dec * H * K / PEAK, H * K * 2 / HBM, T_dec * H * 2 * (n - 1) / LINK) * 1e6
+    out["decode"] = {"T": T_dec, "ours_us": round(ours, 2), "nccl_us": round(base, 2),
+                     "roofline_us": round(roof, 2), "of_roofline": round(roof / ours, 3)}
+    # ---- prefill: GEMM -> reduce-scatter epilogue, reduce + all-gather (eager) vs NCCL
+    xp = torch.randn(T_pre, K, device="cuda").bfloat16()
+    G, rstd = fc.sp_begin(T_pre)
+    G.zero_()
+
+    def ours_pre(i):
+        fc.sp_linear_reduce_scatter(xp, ws[i % nw], G)
+        fc.sp_reduce_allgather(1e-5)
+
+    ours_p = _eager_time(ours_pre)
+    fc.sp_wait()
+    torch.cuda.synchronize()
+    fc.check()
+    ours_p = maxrank(ours_p)
+    yp = torch.empty(T_pre, H, device="cuda", dtype=torch.bfloat16)
+
+    def nccl_pre(i):
+        ext().gemm(yp, xp, ws[i % nw], None, None, 0, -1.0)
+        dist.all_reduce(yp, group=tp.group)
+
+    base_p = maxrank(_eager_time(nccl_pre))
+    rows = -(-T_pre // n)
+    link = (T_pre - rows) * H * 2 + rows * H * 2 * (n - 1)  # reduce-scatter out + all-gather out
+    roof_p = max(2 * T_pre * H * K / PEAK, link / LINK) * 1e6
+    out["prefill"] = {"T": T_pre, "ours_us": round(ours_p, 1), "nccl_us": round(base_p, 1),
+                      "roofline_us": round(roof_p, 1), "of_roofline": round(roof_p / ours_p, 3)}
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    fc.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main(argv=None) -> None:
     import json
 
@@ -198,6 +289,11 @@ def main(argv=None) -> None:
     p.add_argument("--head-dim", type=int, default=128)
     p.add_argument("--splits", type=int, default=0, help="force key splits (0: automatic)")
     p.add_argument("--graph", action="store_true", help="time 20 launches replayed from a CUDA graph")
+    tg = sub.add_parser("tp-gemm", help="row-parallel GEMM + collective, under torchrun (one rank per GPU)")
+    tg.add_argument("--tokens-decode", type=int, default=8)
+    tg.add_argument("--tokens-prefill", type=int, default=4096)
+    tg.add_argument("--hidden", type=int, default=4096)
+    tg.add_argument("--inter", type=int, default=14336)
     s = sub.add_parser("decode-step")
     s.add_argument("model"), s.add_argument("B", type=int), s.add_argument("plen", type=int)
     args = ap.parse_args(argv)
@@ -207,6 +303,8 @@ def main(argv=None) -> None:
                 print(json.dumps(bench_gemm(args.M, args.N, args.K, args.epi, args.graph, sp, args.rms)))
         else:
             print(json.dumps(bench_gemm(args.M, args.N, args.K, args.epi, args.graph, args.splits, args.rms)))
+    elif args.cmd == "tp-gemm":
+        bench_tp_gemm(args.tokens_decode, args.tokens_prefill, args.hidden, args.inter)
     elif args.cmd == "attn-decode":
         print(json.dumps(bench_attn_decode(args.B, args.L, args.Hq, args.Hkv, args.splits)))
     elif args.cmd == "attn-prefill":
