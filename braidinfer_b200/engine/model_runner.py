@@ -128,8 +128,9 @@ class ModelRunner:
     def _decode_splits(self, batch: int, max_kv: Optional[int] = None) -> int:
         L = self.model.layout
         work = max(1, batch * L.kv_heads)
-        # as many key splits as keep every CTA resident in one wave (2 per SM)
-        ns = max(1, min(32, (2 * self.sms) // work))
+        # as many key splits as keep every CTA resident in one wave (2 per SM);
+        # past 16 the split merge costs more than the shorter key loops save
+        ns = max(1, min(16, (2 * self.sms) // work))
         if max_kv is not None:
             ns = max(1, min(ns, -(-max_kv // 64)))
         return ns

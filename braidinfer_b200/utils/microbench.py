@@ -106,7 +106,7 @@ def bench_attn_decode(B: int, L: int, Hq: int, Hkv: int, splits: int = 0, D: int
     q = torch.randn(B, Hq, D, device="cuda").bfloat16()
     cos, sin = ops.build_cos_sin(D, 500000.0, 2 * L + 16, device="cuda")
     sms = torch.cuda.get_device_properties(0).multi_processor_count
-    meta.num_splits = splits or max(1, min(32, (2 * sms) // (B * Hkv), -(-L // 64)))
+    meta.num_splits = splits or max(1, min(16, (2 * sms) // (B * Hkv), -(-L // 64)))
     us = _graph_time(lambda i: ops.attention(q, kvs[i % nc], meta, cos, sin, D ** -0.5))
     return {"kernel": "attn_decode", "B": B, "L": L, "Hq": Hq, "Hkv": Hkv, "splits": meta.num_splits,
             "us": round(us, 2), "kv_TBps": round(byts / us / 1e6, 3), "l2": f"{nc} rotating KV pools (> L2)"}
