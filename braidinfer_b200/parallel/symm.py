@@ -67,8 +67,8 @@ class FusedComm:
         data = 2 * tp.size * max_tokens * hidden * 2
         self.flags_off = align(data)
         off = self.flags_off + align(8 * tp.size)
-        # per-(source, 128-feature tile) flags of the in-GEMM all-reduce
-        self.max_tiles = -(-hidden // 128)
+        # per-(source, output tile) flags of the in-GEMM all-reduce: 128 features x up to 4 token tiles
+        self.max_tiles = -(-hidden // 128) * 4
         self.tile_flags_off = off
         off += align(8 * tp.size * self.max_tiles)
         # sequence-parallel prefill region

@@ -68,7 +68,7 @@ def _eager_time(fn, n: int = 10) -> float:
 
 
 def bench_gemm(M: int, N: int, K: int, epi: int = 0, graph: bool = False, splits: int = -1,
-               rms: bool = False) -> dict:
+               rms: bool = False, bn: int = 0) -> dict:
     from ..ops._ext import ext
 
     nc = _copies((N + M) * K * 2)  # weight and activation copies rotate: HBM, not L2
@@ -77,10 +77,12 @@ def bench_gemm(M: int, N: int, K: int, epi: int = 0, graph: bool = False, splits
     ws = [w0] + [w0.clone() for _ in range(nc - 1)]
     out = torch.empty(M, N // 2 if epi else N, device="cuda", dtype=torch.bfloat16)
     ext().gemm_force_splits(splits)
+    ext().gemm_force_bn(bn)
     fn = lambda i: ext().gemm(out, xs[i % nc], ws[i % nc], None, None, epi, 1e-5 if rms else -1.0)  # noqa: E731
     us = (_graph_time if graph else _eager_time)(fn)
     ext().gemm_force_splits(-1)
-    return {"kernel": "gemm_tcgen05", "M": M, "N": N, "K": K, "epi": epi, "rms": rms, "splits": splits,
+    ext().gemm_force_bn(0)
+    return {"kernel": "gemm_tcgen05", "M": M, "N": N, "K": K, "epi": epi, "rms": rms, "splits": splits, "bn": bn,
             "us": round(us, 2), "weight_TBps": round(N * K * 2 / us / 1e6, 3),
             "TFLOPS": round(2 * M * N * K / us / 1e6, 1), "l2": f"{nc} rotating input copies (> L2)"}
 
@@ -277,6 +279,7 @@ def main(argv=None) -> None:
     g.add_argument("--splits", type=int, default=-1, help="force the split-K factor (-1: heuristic)")
     g.add_argument("--rms", action="store_true", help="fused input RMSNorm")
     g.add_argument("--sweep-splits", action="store_true", help="time every split-K factor 1..16")
+    g.add_argument("--bn", type=int, default=0, help="force the decode token-tile width 16/32/64")
     a = sub.add_parser("attn-decode")
     for n in ("B", "L", "Hq", "Hkv"):
         a.add_argument(n, type=int)
@@ -300,9 +303,10 @@ def main(argv=None) -> None:
     if args.cmd == "gemm":
         if args.sweep_splits:
             for sp in (0, 1, 2, 3, 4, 6, 8, 12, 16):
-                print(json.dumps(bench_gemm(args.M, args.N, args.K, args.epi, args.graph, sp, args.rms)))
+                print(json.dumps(bench_gemm(args.M, args.N, args.K, args.epi, args.graph, sp, args.rms, args.bn)))
         else:
-            print(json.dumps(bench_gemm(args.M, args.N, args.K, args.epi, args.graph, args.splits, args.rms)))
+            print(json.dumps(bench_gemm(args.M, args.N, args.K, args.epi, args.graph, args.splits, args.rms,
+                                        args.bn)))
     elif args.cmd == "tp-gemm":
         bench_tp_gemm(args.tokens_decode, args.tokens_prefill, args.hidden, args.inter)
     elif args.cmd == "attn-decode":

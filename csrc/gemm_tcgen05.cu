@@ -428,7 +428,7 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
             __threadfence_system();
             for (int p = 0; p < ps.tp; ++p)
               st_release_sys_u64(reinterpret_cast<uint64_t*>(reinterpret_cast<char*>(ps.peers[p]) + ps.tile_flags_off) +
-                                     (size_t)ps.rank * ps.max_tiles + m_tile,
+                                     (size_t)ps.rank * ps.max_tiles + tile,
                                  epoch + 1);
           }
           int* s_ok = s_flag;
@@ -436,7 +436,7 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
           named_bar_sync(1, 128);
           if (et < ps.tp) {
             const uint64_t* f = reinterpret_cast<const uint64_t*>(reinterpret_cast<const char*>(ps.peers[ps.rank]) +
-                                                                  ps.tile_flags_off) + (size_t)et * ps.max_tiles + m_tile;
+                                                                  ps.tile_flags_off) + (size_t)et * ps.max_tiles + tile;
             const uint64_t t0 = globaltimer_ns();
             while (ld_acquire_sys_u64(f) < epoch + 1) {
               if (globaltimer_ns() - t0 > ps.timeout_ns) {
@@ -453,26 +453,27 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
           }
           named_bar_sync(1, 128);
           if (*s_ok && m < args.M) {
-            // 8 tokens x up to 8 sources of this feature per pass, all loads in flight
+            // this tile's tokens [n0, t_end): 8 tokens x up to 8 sources per pass, loads in flight
             const __nv_bfloat16* recv = reinterpret_cast<const __nv_bfloat16*>(ps.peers[ps.rank]) +
                                         (size_t)slot * ps.tp * ps.maxT * args.M + m;
-            for (int t0 = 0; t0 < args.N; t0 += 8) {
+            const int t_end = min(args.N, n0 + BN);
+            for (int t0 = n0; t0 < t_end; t0 += 8) {
               __nv_bfloat16 pv[8][8];
               float res[8];
 #pragma unroll
               for (int src = 0; src < 8; ++src)
 #pragma unroll
                 for (int j = 0; j < 8; ++j)
-                  pv[src][j] = (src < ps.tp && t0 + j < args.N)
+                  pv[src][j] = (src < ps.tp && t0 + j < t_end)
                                    ? __ldcv(recv + ((size_t)src * ps.maxT + t0 + j) * args.M)
                                    : __float2bfloat16(0.f);
 #pragma unroll
               for (int j = 0; j < 8; ++j)
-                res[j] = (args.residual && t0 + j < args.N) ? bf2f(args.residual[(size_t)(t0 + j) * args.ldr + m])
+                res[j] = (args.residual && t0 + j < t_end) ? bf2f(args.residual[(size_t)(t0 + j) * args.ldr + m])
                                                             : 0.f;
 #pragma unroll
               for (int j = 0; j < 8; ++j) {
-                if (t0 + j >= args.N) continue;
+                if (t0 + j >= t_end) continue;
                 float acc = 0.f;
 #pragma unroll
                 for (int src = 0; src < 8; ++src) acc += bf2f(pv[src][j]);
@@ -701,6 +702,9 @@ unsigned long long* next_span() {
 static int g_forced_splits = -1;
 // Tuning: force the split-K factor of later tile-per-CTA launches (0 = heuristic, -1 = environment).
 void gemm_force_splits(int64_t n) { g_forced_splits = (int)n; }
+static int g_forced_bn = 0;
+// Tuning: force the token-tile width (16/32/64) of later decode-mode launches (0 = heuristic).
+void gemm_force_bn(int64_t n) { g_forced_bn = (int)n; }
 
 static unsigned long long* g_trace = nullptr;
 // Profiling: record per-CTA phase timestamps of subsequent GEMM launches into
@@ -760,6 +764,36 @@ static int64_t run_gemm(GemmArgs& a, const torch::Tensor& x, const torch::Tensor
   int BN, m_tiles, n_tiles;
   if (swap) {
     BN = T <= 16 ? 16 : T <= 32 ? 32 : 64;
+    if (T > 32) {
+      // 33-64 tokens: several narrow token tiles beat one 64-wide tile unless the
+      // weight alone fills the machine (measured on B200, HBM-resident weights):
+      // the smallest width whose grid fits one wave with at most 32 K-blocks per
+      // CTA, else the width (of those fitting one wave) with the fewest K-blocks
+      // per CTA.
+      const int slots2 = gemm_num_sms() * 2, mt = (F + BM - 1) / BM;
+      auto kb_per_cta = [&](int bn) {
+        const int tiles = mt * ((T + bn - 1) / bn);
+        const int sp = std::max(1, std::min({slots2 / tiles, kb_total / 2, 16, 256 / bn}));
+        return (kb_total + sp - 1) / sp;
+      };
+      int pick = 0;
+      for (int bn : {16, 32}) {
+        if (mt * ((T + bn - 1) / bn) <= slots2 && kb_per_cta(bn) <= 32) {
+          pick = bn;
+          break;
+        }
+      }
+      if (!pick) {
+        int best = 1 << 30;
+        for (int bn : {16, 32, 64})
+          if (mt * ((T + bn - 1) / bn) <= slots2 && kb_per_cta(bn) < best) {
+            best = kb_per_cta(bn);
+            pick = bn;
+          }
+      }
+      if (pick) BN = pick;
+    }
+    if (g_forced_bn == 16 || g_forced_bn == 32 || g_forced_bn == 64) BN = g_forced_bn;
     a.M = F;
     a.N = T;
     m_tiles = (F + BM - 1) / BM;
@@ -772,8 +806,9 @@ static int64_t run_gemm(GemmArgs& a, const torch::Tensor& x, const torch::Tensor
     n_tiles = (F + BN - 1) / BN;
   }
   const int tiles = m_tiles * n_tiles;
-  // reduce-scatter epilogue: partial tiles this rank (as row owner) receives from every source
-  int64_t arrivals = 0;
+  // reduce-scatter epilogue: partial tiles this rank (as row owner) receives from every source;
+  // push epilogue (epi 3): every output tile bumps each peer's counter once
+  int64_t arrivals = a.epi == 3 ? tiles : 0;
   if (a.epi == 4) {
     TORCH_CHECK(a.sp.peers != nullptr && a.sp.H == F, "gemm: epi 4 needs sequence-parallel params");
     const int r0 = a.sp.rank * a.sp.rows_per_rank, r1 = std::min(T, r0 + a.sp.rows_per_rank);
@@ -946,7 +981,8 @@ void gemm_allreduce_add(torch::Tensor residual, torch::Tensor x, torch::Tensor w
                         int64_t flags_off, int64_t tile_flags_off, int64_t max_tiles, int64_t rank, int64_t tp,
                         int64_t maxT, torch::Tensor epoch_state, torch::Tensor status, double timeout_s) {
   TORCH_CHECK(x.size(0) <= 64 && x.size(0) <= maxT, "gemm_allreduce_add: decode shapes only (<= 64 tokens)");
-  TORCH_CHECK(w.size(0) <= max_tiles * BM, "gemm_allreduce_add: too many output tiles for the flag area");
+  TORCH_CHECK((w.size(0) + BM - 1) / BM * ((x.size(0) + 15) / 16) <= max_tiles,
+              "gemm_allreduce_add: too many output tiles for the flag area");
   TORCH_CHECK(tp >= 1 && tp <= 8, "gemm_allreduce_add: one NVLink domain of at most 8 ranks");
   TORCH_CHECK(residual.is_contiguous() && residual.size(0) == x.size(0) && residual.size(1) == w.size(0));
   GemmArgs a{};
@@ -980,10 +1016,7 @@ int64_t gemm_push(torch::Tensor x, torch::Tensor w, torch::Tensor peers, int64_t
   a.push.rank = rank;
   a.push.tp = tp;
   a.push.maxT = maxT;
-  run_gemm(a, x, w, false);
-  const int T = x.size(0), F = w.size(0);
-  const int BN = T <= 16 ? 16 : T <= 32 ? 32 : 64;
-  return (int64_t)((F + BM - 1) / BM) * ((T + BN - 1) / BN);
+  return run_gemm(a, x, w, false);
 }
 }  // namespace braid
 

@@ -45,7 +45,7 @@ def _w_allreduce(rank, world, port, q):
         from braidinfer_b200.parallel.state import init_tp
         from braidinfer_b200.parallel.symm import FusedComm
         tp = init_tp(world)
-        fc = FusedComm(tp, 1024, torch.device("cuda", rank), max_tokens=16, timeout_s=5.0)
+        fc = FusedComm(tp, 1024, torch.device("cuda", rank), max_tokens=64, timeout_s=5.0)
         errs = []
         for it in range(6):
             g = torch.Generator(device="cuda").manual_seed(100 * it + rank)
@@ -62,7 +62,7 @@ def _w_allreduce(rank, world, port, q):
         # between, the two-kernel form (push epilogue + reduce kernel)
         w = (torch.randn(1024, 512, device="cuda", generator=torch.Generator(device="cuda").manual_seed(rank)) * 0.05).bfloat16()
         for it, (T, fused) in enumerate([(5, True), (1, True), (16, False), (8, True), (13, True), (3, False),
-                                         (16, True)]):
+                                         (16, True), (40, True), (64, False), (64, True), (37, False)]):
             xw = torch.randn(T, 512, device="cuda", generator=torch.Generator(device="cuda").manual_seed(50 + it + 7 * rank)).bfloat16()
             part = (xw.float() @ w.float().t()).bfloat16()
             ref = part.float().clone()
