@@ -405,7 +405,7 @@ def run_reference(args) -> None:
 # ------------------------------------------------------------------ TTFT
 def run_ttft(args) -> None:
     """TTFT of a RAG-style composition: a 128-token system chunk plus 3 of 16
-    registered 1024-token contexts plus a 64-token query (
+    registered 1024-token contexts plus a 64-token query (the cascade/RAG configuration,
     TinyLlama-1.1B architecture), with the chunks' KV cached, against a full
     prefill of the same 3264 tokens.  Device time (CUDA events) through the
     public API, max of ranks not needed (one GPU)."""

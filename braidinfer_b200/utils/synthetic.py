@@ -15,7 +15,7 @@ from typing import Optional
 import torch
 
 PRESETS = {
-    # CPU fp32 plumbing model
+    # CPU fp32 plumbing/correctness model (2 layers, hidden 256)
     "tiny-llama": dict(model_type="llama", hidden_size=256, num_hidden_layers=2, num_attention_heads=4,
                        num_key_value_heads=2, head_dim=64, intermediate_size=688, vocab_size=1024,
                        rms_norm_eps=1e-6, rope_theta=10000.0, max_position_embeddings=4096,

@@ -1,6 +1,6 @@
 """Engine semantics on CPU (fp32) against the independent oracle.
 
-tiny Llama (2 layers, hidden 256, 4q/2kv heads, head 64,
+The CPU correctness configuration: tiny Llama (2 layers, hidden 256, 4q/2kv heads, head 64,
 SwiGLU 688, vocab 1024), chunks of 32/48/64/16 random tokens (seed 0),
 cascade with differential RoPE vs the concatenated prompt under the
 block-causal mask implied by independent chunk caching; greedy decode of 16
