@@ -101,7 +101,13 @@ class LLMEngine:
         self._closed = True
         try:
             self.release_all_retained_sequences()
+            # graphs may hold NCCL calls (TP): release them before the process group goes away
             self.model_runner.graphs.clear()
+            self.model_runner.prefill_graphs.clear()
+            if self.model_runner.device.type == "cuda":
+                import torch
+
+                torch.cuda.synchronize(self.model_runner.device)
         except Exception:
             pass
 
