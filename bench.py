@@ -326,80 +326,27 @@ def run_cascade(args) -> None:
 
 # ---------------------------------------------------------------- reference
 def run_reference(args) -> None:
+    """The unmodified reference through its public API (``baseline/ref_tp/harness.py``):
+    one GPU, or its NCCL all-reduce tensor-parallel build under torchrun.
+    Nothing from ``braidinfer_b200`` is imported on this path."""
     n = args.gpus
     rank = int(os.environ.get("RANK", "0"))
-    if n > 1:
+    if not os.path.isdir(os.path.join(ROOT, "baseline", "_ref", "braidinfer")):
         if rank == 0:
-            print(json.dumps({"impl": "reference", "unavailable":
-                              "the reference is single-GPU: no live tensor-parallel path (its only collective is "
-                              "dead code in braidinfer/layers/linear_distributed.py)"}), flush=True)
+            print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref not installed"}), flush=True)
         return
-    ref = os.path.join(ROOT, "baseline", "_ref")
-    if not os.path.isdir(os.path.join(ref, "braidinfer")):
-        print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref not installed"}), flush=True)
+    sys.path.insert(0, os.path.join(ROOT, "baseline", "ref_tp"))
+    import harness
+
+    if args.model not in harness.ARCH:
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": f"no reference harness for {args.model}"}),
+                  flush=True)
         return
-    sys.path.insert(0, ref)
-    import torch
-
-    from braidinfer import LLM, SamplingParams  # the unmodified reference
-    from braidinfer.engine.errors import ModelLoadError
-
-    kw = dict(num_kvcache_blocks=-(-(args.prompt_len + args.warmup + args.steps + 64) // 256) + 4,
-              max_model_len=args.prompt_len + args.warmup + args.steps + 64)
-    # Model construction happens before any weight is read, so try it on the
-    # config-only directory first and report an incompatibility without
-    # writing the 16 GB checkpoint.
-    try:
-        LLM(make_config_dir(args.model, with_weights=False), **kw)
-    except ModelLoadError as e:
-        msg = str(e)
-        if "Failed to create model instance" in msg:
-            print(json.dumps({"impl": "reference", "unavailable":
-                              f"reference model construction fails in this image: {msg} (its lru_cache'd "
-                              "get_rope receives transformers 5.5's rope_scaling dict)"}), flush=True)
-            return
-    except Exception:
-        pass
-    d = make_config_dir(args.model, with_weights=True)
-    # The reference raises NotImplementedError for batch > 1
-    # (braidinfer/layers/attention.py:146-147), so the batch's requests run one
-    # after another through its public generate(stream=True) API.
-    llm = LLM(d, **kw)
-    prompts = prompts_for(args.batch, args.prompt_len, llm.config.hf_config.vocab_size)
-    sp = SamplingParams(temperature=0.0, max_tokens=args.warmup + args.steps + 1, ignore_eos=True)
-    import contextlib
-    import io
-
-    dev_ms, wall, toks = 0.0, 0.0, 0
-    with ClockSampler(torch.cuda.current_device()) as clocks:
-        for p in prompts:
-            evs, times = [], []
-            with contextlib.redirect_stdout(io.StringIO()):
-                for item in llm.generate(p, sp, stream=True):
-                    e = torch.cuda.Event(enable_timing=True)
-                    e.record()
-                    evs.append(e)
-                    times.append(time.perf_counter())
-            torch.cuda.synchronize()
-            # token records: 0..warmup-1 untimed; then `steps` timed intervals
-            a, b = args.warmup, args.warmup + args.steps
-            if len(evs) <= b:
-                raise RuntimeError("reference produced fewer tokens than requested")
-            dev_ms += evs[a].elapsed_time(evs[b])
-            wall += times[b] - times[a]
-            toks += args.steps
-    value = toks / (dev_ms / 1e3)
-    print(json.dumps({
-        "metric": f"decode tok/s (bs{args.batch}) {args.model} TP1", "value": round(value, 2), "unit": "tokens/s",
-        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(dev_ms / args.steps / args.batch, 4), "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": round(value / PUBLISHED_BS8, 3), "dtype": "bf16",
-        "data": "synthetic token ids (seed 3), random-init N(0,0.02) weights",
-        "config": {"model": args.model, "global_batch": args.batch, "seq_len": args.prompt_len, "parallelism": "tp1",
-                   "note": "reference cannot batch: requests decoded one at a time (lower bound)"},
-        "clocks": clocks.summary(), "e2e": {"value": round(toks / wall, 2), "unit": "tokens/s",
-                                            "h2d_bytes_per_step": None, "d2h_bytes_per_step": None},
-        "impl": "reference"}), flush=True)
+    if n == 1:
+        harness.run_tp1(args, ClockSampler, PUBLISHED_BS8)
+    else:
+        harness.run_tp(args, ClockSampler, PUBLISHED_BS8)
 
 
 # ------------------------------------------------------------------ TTFT

@@ -19,17 +19,21 @@
 // K-slices (never with more scratch).
 //
 // Set-up: the first call on each device looks up the device address of the
-// scratch array (with that device current) and clears it; make that first call
-// before any stream capture.  Every later call reuses the same array and
-// clears the parts that must start at zero (tile counters, error word) on the
+// scratch array (with that device current), clears it on the caller's stream
+// and waits for that clear; make that first call before any stream capture.
+// Every later call reuses the same array and clears the tile counters on the
 // caller's stream.  All calls on one device share that device's array, so two
 // calls that can execute at the same time on one device (for example on two
 // streams with no ordering between them) race on it and must be serialised
 // by the caller; calls on different devices use different copies.
 //
-// Returns 0 on success; otherwise a nonzero code, and
-// braid_gemm_noalloc_last_error() describes the problem.  Nothing here calls
-// cudaMalloc, cudaFree, or any allocating library routine.
+// Returns 0 once the kernel is launched; otherwise a nonzero code, and
+// braid_gemm_noalloc_last_error() describes the problem.  Problems the kernel
+// meets on the GPU (a bounded pipeline wait that ran out) are recorded in the
+// array's error word, which stays set until braid_gemm_noalloc_check_error()
+// reads it: that call waits for `stream`, returns the word (0 = no error,
+// -1 = the read itself failed) and clears it.  Nothing here calls cudaMalloc,
+// cudaFree, or any allocating library routine.
 #pragma once
 
 #ifdef __cplusplus
@@ -43,6 +47,7 @@ extern "C" {
 int braid_gemm_noalloc(void* out, const void* x, const void* w, const void* bias, const void* residual, int T,
                        int N, int K, int ldo, int ldx, int ldw, int ldr, float rs_eps, void* stream);
 const char* braid_gemm_noalloc_last_error(void);
+int braid_gemm_noalloc_check_error(void* stream);
 
 #ifdef __cplusplus
 }

@@ -30,6 +30,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <atomic>
 #include <mutex>
 #include <unordered_map>
 #include <vector>
@@ -1037,7 +1038,11 @@ struct Scratch {
 static __device__ __align__(256) Scratch g_scratch;
 
 constexpr int kMaxDevices = 64;
-static Scratch* g_addr[kMaxDevices] = {};
+// Device address of g_scratch per device (set once under g_setup_mu).
+static std::atomic<Scratch*> g_addr[kMaxDevices];
+// Per device: bit i set once the kernel for token-tile width 16 << i has its
+// shared-memory attribute (set under g_setup_mu).
+static std::atomic<unsigned> g_attr_done[kMaxDevices];
 static std::mutex g_setup_mu;
 static thread_local char g_msg[256] = "";
 
@@ -1059,13 +1064,42 @@ static CUtensorMap encode(const void* ptr, int64_t rows, int64_t cols, int64_t l
   return m;
 }
 
+// First use on `dev` (current): resolve the array's device address and clear
+// it on the caller's stream, then wait for the clear, so no later launch on
+// any stream can overtake it.
+static Scratch* setup(int dev, cudaStream_t st, int* code) {
+  Scratch* sc = g_addr[dev].load(std::memory_order_acquire);
+  if (sc != nullptr) return sc;
+  std::lock_guard<std::mutex> g(g_setup_mu);
+  sc = g_addr[dev].load(std::memory_order_relaxed);
+  if (sc != nullptr) return sc;
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_scratch);
+  if (e == cudaSuccess && p != nullptr) e = cudaMemsetAsync(p, 0, sizeof(Scratch), st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess || p == nullptr) {
+    *code = fail(6, cudaGetErrorString(e));
+    return nullptr;
+  }
+  sc = static_cast<Scratch*>(p);
+  g_addr[dev].store(sc, std::memory_order_release);
+  return sc;
+}
+
 template <int BN>
-static cudaError_t launch_plain(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, dim3 grid,
+static cudaError_t launch_plain(int dev, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, dim3 grid,
                                 cudaStream_t st) {
   using S = GemmSmem<BN, 4>;
   auto kern = gemm_tcgen05_kernel<BN, 4>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL);
-  if (e != cudaSuccess) return e;
+  const unsigned bit = BN == 16 ? 1u : BN == 32 ? 2u : 4u;
+  if (!(g_attr_done[dev].load(std::memory_order_acquire) & bit)) {
+    std::lock_guard<std::mutex> g(g_setup_mu);
+    if (!(g_attr_done[dev].load(std::memory_order_relaxed) & bit)) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL);
+      if (e != cudaSuccess) return e;
+      g_attr_done[dev].fetch_or(bit, std::memory_order_release);
+    }
+  }
   kern<<<grid, 192, S::TOTAL, st>>>(ta, tb, a);
   return cudaGetLastError();
 }
@@ -1074,6 +1108,20 @@ static cudaError_t launch_plain(const CUtensorMap& ta, const CUtensorMap& tb, co
 }  // namespace braid
 
 extern "C" const char* braid_gemm_noalloc_last_error(void) { return braid::noalloc::g_msg; }
+
+extern "C" int braid_gemm_noalloc_check_error(void* stream) {
+  using namespace braid::noalloc;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return -1;
+  Scratch* sc = g_addr[dev].load(std::memory_order_acquire);
+  if (sc == nullptr) return 0;  // never called on this device
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int h = 0;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return -1;
+  if (cudaMemcpy(&h, &sc->err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+  if (h != 0 && cudaMemset(&sc->err, 0, sizeof(int)) != cudaSuccess) return -1;
+  return h;
+}
 
 extern "C" int braid_gemm_noalloc(void* out, const void* x, const void* w, const void* bias, const void* residual,
                                   int T, int N, int K, int ldo, int ldx, int ldw, int ldr, float rs_eps,
@@ -1087,23 +1135,14 @@ extern "C" int braid_gemm_noalloc(void* out, const void* x, const void* w, const
     return fail(3, "K and the row strides must be multiples of 8 and at least the row length");
   if (((uintptr_t)x | (uintptr_t)w) & 15) return fail(4, "x and w must be 16-byte aligned");
   if (residual != nullptr && ldr < N) return fail(3, "residual stride shorter than N");
+  const int m_tiles = (N + BM - 1) / BM;
+  if (m_tiles > BRAID_NOALLOC_MAX_TILES) return fail(10, "N exceeds the tile-counter capacity (2097152 rows)");
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return fail(5, "no current CUDA device");
-  Scratch* sc = g_addr[dev];
-  if (sc == nullptr) {
-    // Set-up on this device (it is current): resolve the array's device address.
-    std::lock_guard<std::mutex> g(g_setup_mu);
-    if (g_addr[dev] == nullptr) {
-      void* p = nullptr;
-      cudaError_t e = cudaGetSymbolAddress(&p, g_scratch);
-      if (e != cudaSuccess || p == nullptr) return fail(6, cudaGetErrorString(e));
-      e = cudaMemset(p, 0, sizeof(Scratch));
-      if (e != cudaSuccess) return fail(6, cudaGetErrorString(e));
-      g_addr[dev] = static_cast<Scratch*>(p);
-    }
-    sc = g_addr[dev];
-  }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int code = 0;
+  Scratch* sc = setup(dev, st, &code);
+  if (sc == nullptr) return code;
   GemmArgs a{};
   a.K = K;
   a.swap = 1;
@@ -1119,15 +1158,16 @@ extern "C" int braid_gemm_noalloc(void* out, const void* x, const void* w, const
   a.rs_ld = ldx;
   a.rs_eps = rs_eps;
   const int BN = T <= 16 ? 16 : T <= 32 ? 32 : 64;
-  const int m_tiles = (N + BM - 1) / BM;
   const int tiles = m_tiles;
   const int kb_total = (K + BK - 1) / BK;
+  // same split-K rule as the regular entry point (one resident wave, at most
+  // 16 slices and 256 / BN partial columns for the last CTA to sum) ...
   int splits = 1;
   const int slots = gemm_num_sms() * 2;
-  if (tiles < slots) splits = std::max(1, std::min({slots / tiles, kb_total / 2, 32}));
-  // never more scratch than the fixed array holds
-  while (splits > 1 && ((size_t)tiles * splits * BM * BN * 4 > BRAID_NOALLOC_PARTIAL_BYTES || tiles > BRAID_NOALLOC_MAX_TILES))
-    --splits;
+  if (tiles < slots) splits = std::max(1, std::min({slots / tiles, kb_total / 2, 16}));
+  splits = std::max(1, std::min(splits, 256 / BN));
+  // ... and never more partial space than the fixed array holds
+  while (splits > 1 && (size_t)tiles * splits * BM * BN * 4 > BRAID_NOALLOC_PARTIAL_BYTES) --splits;
   int kbps = (kb_total + splits - 1) / splits;
   splits = (kb_total + kbps - 1) / kbps;
   a.splits = splits;
@@ -1135,9 +1175,9 @@ extern "C" int braid_gemm_noalloc(void* out, const void* x, const void* w, const
   a.ws = sc->partial;
   a.counters = sc->counters;
   a.err = &sc->err;
-  // counters and the error word must start at zero for this call
-  if (cudaMemsetAsync(sc->counters, 0, sizeof(int) * (splits > 1 ? tiles : 1), st) != cudaSuccess ||
-      cudaMemsetAsync(&sc->err, 0, sizeof(int), st) != cudaSuccess)
+  // the tile counters must start at zero (the last CTA of each tile re-arms
+  // its counter; clearing also recovers from a call that timed out)
+  if (splits > 1 && cudaMemsetAsync(sc->counters, 0, sizeof(int) * tiles, st) != cudaSuccess)
     return fail(7, "clearing the scratch counters failed");
   bool ok1 = false, ok2 = false;
   CUtensorMap ta = encode(w, N, K, ldw, BM, &ok1);
@@ -1146,9 +1186,9 @@ extern "C" int braid_gemm_noalloc(void* out, const void* x, const void* w, const
   dim3 grid(m_tiles, 1, splits);
   cudaError_t e;
   switch (BN) {
-    case 16: e = launch_plain<16>(ta, tb, a, grid, st); break;
-    case 32: e = launch_plain<32>(ta, tb, a, grid, st); break;
-    default: e = launch_plain<64>(ta, tb, a, grid, st); break;
+    case 16: e = launch_plain<16>(dev, ta, tb, a, grid, st); break;
+    case 32: e = launch_plain<32>(dev, ta, tb, a, grid, st); break;
+    default: e = launch_plain<64>(dev, ta, tb, a, grid, st); break;
   }
   if (e != cudaSuccess) return fail(9, cudaGetErrorString(e));
   return 0;

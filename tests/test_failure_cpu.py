@@ -26,7 +26,9 @@ def _worker(rank, world, port, mode, q):
     import torch.distributed as dist
 
     from braidinfer_b200.parallel.health import Heartbeat
-    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=3))
+    # The rendezvous gets a generous timeout (spawned ranks start at different
+    # times); detection itself rests on the 2 s heartbeat deadline.
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=60))
     hb = Heartbeat(timeout_s=2.0)
     try:
         for step in range(4):
