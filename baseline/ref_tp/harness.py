@@ -236,8 +236,9 @@ def _decode_requests(llm, prompts, sp, warmup: int, steps: int):
 def _prompts(batch: int, plen: int, vocab: int, seed: int = 3):
     import torch
 
-    g = torch.Generator().manual_seed(seed)
-    return [torch.randint(3, vocab, (plen,), generator=g).tolist() for _ in range(batch)]
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    # the reference sets the default device to CUDA; these ids are built on the host
+    return [torch.randint(3, vocab, (plen,), generator=g, device="cpu").tolist() for _ in range(batch)]
 
 
 def _line(args, n, dev_ms, wall, toks, clocks, published, note):
@@ -270,8 +271,8 @@ def run_tp1(args, clock_sampler, published: float) -> None:
     from braidinfer import LLM, SamplingParams  # the unmodified reference
 
     d = write_checkpoint(os.path.join(tempfile.gettempdir(), f"braid_ref_{args.model}_tp1"), args.model)
-    llm = LLM(d, **_engine_kwargs(args))
     prompts = _prompts(args.batch, args.prompt_len, ARCH[args.model]["vocab_size"])
+    llm = LLM(d, **_engine_kwargs(args))
     sp = SamplingParams(temperature=0.0, max_tokens=args.warmup + args.steps + 1, ignore_eos=True)
     with clock_sampler(torch.cuda.current_device()) as clocks:
         e0 = time.time()
@@ -305,8 +306,8 @@ def run_tp(args, clock_sampler, published: float) -> None:
     if rank == 0:
         write_checkpoint(d, args.model, tp=n)
     dist.barrier()
-    llm = LLM(d, **_engine_kwargs(args))
     prompts = _prompts(args.batch, args.prompt_len, ARCH[args.model]["vocab_size"])
+    llm = LLM(d, **_engine_kwargs(args))
     sp = SamplingParams(temperature=0.0, max_tokens=args.warmup + args.steps + 1, ignore_eos=True)
     dist.barrier()
     torch.cuda.synchronize()

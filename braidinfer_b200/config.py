@@ -143,6 +143,7 @@ class Config:
     seed: int = 0
     load_weights: bool = True     # False: random-init weights (synthetic benchmarks)
     init_std: float = 0.02
+    init_k_norm_range: Optional[float] = None  # random init: Qwen3 k_norm weights uniform in [-r, r]
     spec: Optional[ModelSpec] = field(default=None, repr=False)
 
     def __post_init__(self):

@@ -76,7 +76,7 @@ class ModelRunner:
 
             load_model(self.model, config.model)
         else:
-            self.model.random_init(seed=config.seed, std=config.init_std)
+            self.model.random_init(seed=config.seed, std=config.init_std, k_norm_range=config.init_k_norm_range)
         self.model.finalize()
         log.info("model ready in %.1fs", time.time() - t0)
         self.page_manager: Optional[PageManager] = None

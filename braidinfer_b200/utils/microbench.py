@@ -4,6 +4,7 @@
     python -m braidinfer_b200.utils.microbench attn-decode B L HQ HKV [--splits S]
     python -m braidinfer_b200.utils.microbench attn-prefill L HQ HKV [--batch B] [--ctx C] [--head-dim D] [--splits S]
     python -m braidinfer_b200.utils.microbench decode-step MODEL B PROMPT_LEN
+    [torchrun --nproc-per-node N -m] braidinfer_b200.utils.microbench decode-trace MODEL B PROMPT_LEN [--out F]
     torchrun --nproc-per-node N -m braidinfer_b200.utils.microbench tp-gemm [--tokens-decode 8] ...
 
 ``decode-step`` runs one eager decode step of a random-init model between
@@ -177,6 +178,125 @@ def decode_step(model: str, B: int, plen: int) -> None:
     torch.cuda.cudart().cudaProfilerStop()
 
 
+def decode_trace(model: str, B: int, plen: int, replays: int = 5, out_path: str = "") -> dict:
+    """Per-launch timeline of one graph-replayed decode step (one GPU, or every
+    rank under torchrun with ``tensor_parallel_size`` = world size).
+
+    Every native launch of the captured step records, on the device, its first
+    CTA start, the first moment a CTA passed its dependency wait (for the
+    collectives: the bounded wait for the peers) and its last CTA end
+    (``span_trace``).  Per launch name it reports, per step, the summed
+    ``busy`` time (dependency release to last CTA end: the launch's share of
+    the critical path), ``lead`` (start to release: prologue overlapped with
+    the predecessor, or, for a collective, the wait for the slowest peer) and
+    ``release`` gaps (previous launch's end to this launch's release).  Under
+    TP each rank reports; rank 0 prints all and the step time of each.
+    """
+    import datetime
+    import json
+    import os
+    import tempfile
+
+    import torch.distributed as dist
+
+    from .. import LLM, SamplingParams
+    from ..ops._ext import ext
+    from .synthetic import make_checkpoint
+
+    n = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if n > 1 and not dist.is_initialized():
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    rank = dist.get_rank() if n > 1 else 0
+    d = os.path.join(tempfile.gettempdir(), f"braid_mb_{model}")
+    if rank == 0 and not os.path.exists(os.path.join(d, "config.json")):
+        make_checkpoint(d, model, write_weights=False)
+    if n > 1:
+        dist.barrier()
+    page = 256
+    max_len = plen + 64 + replays + 16
+    llm = LLM(d, load_weights=False, tensor_parallel_size=n, max_num_seqs=B, max_model_len=max_len,
+              num_kvcache_blocks=B * math.ceil(max_len / page) + 8, kvcache_block_size=page,
+              max_graph_batch=B, max_num_batched_tokens=max(16384, max_len))
+    g = torch.Generator().manual_seed(3)
+    sp = SamplingParams(temperature=0, max_tokens=replays + 16, ignore_eos=True)
+    for _ in range(B):
+        llm.add_request(torch.randint(3, llm.config.spec.vocab_size, (plen,), generator=g).tolist(), sp)
+    while llm.scheduler.waiting:
+        llm.step()
+    for _ in range(3):
+        llm.step()
+    runner = llm.model_runner
+    C = ext()
+    buf = torch.zeros(4 * 4096, dtype=torch.int64, device="cuda")
+    runner.graphs.pop(B, None)
+    C.span_trace(buf)
+    llm.step()  # re-captures the bucket with span slots baked into the launches
+    C.span_trace(torch.empty(0, dtype=torch.int64))
+    names = C.span_names()
+    L = runner.graphs[B].launches
+    # the capture runs the step twice eagerly before recording it: the graph's slots are the last L
+    base = len(names) - L
+    names = names[base:]
+    MAXU = -1  # all bits set: the initial value for the atomicMin fields
+    steps = []
+    for _ in range(replays):
+        v = buf.view(-1, 4)
+        v[base:base + L, 0] = MAXU
+        v[base:base + L, 1] = MAXU
+        v[base:base + L, 2] = 0
+        torch.cuda.synchronize()
+        if n > 1:
+            dist.barrier()
+        llm.step()
+        torch.cuda.synchronize()
+        a = v[base:base + L, :3].cpu().numpy().astype("uint64")
+        steps.append(a)
+    per = {}
+    step_us = []
+    for a in steps:
+        t0 = int(a[:, 0].min())
+        start = (a[:, 0] - t0).astype("float64") / 1e3
+        waited = a[:, 1].copy()
+        waited[waited == (2 ** 64 - 1)] = a[waited == (2 ** 64 - 1), 0]
+        waited = (waited - t0).astype("float64") / 1e3
+        end = (a[:, 2] - t0).astype("float64") / 1e3
+        step_us.append(float(end.max()))
+        for i, nm in enumerate(names):
+            r = per.setdefault(nm, {"count": 0, "busy_us": 0.0, "lead_us": 0.0, "release_us": 0.0})
+            r["count"] += 1
+            r["busy_us"] += max(0.0, end[i] - waited[i])
+            r["lead_us"] += max(0.0, waited[i] - start[i])
+            if i:
+                r["release_us"] += max(0.0, waited[i] - end[i - 1])
+    R = len(steps)
+    for r in per.values():
+        r["count"] //= R
+        for k in ("busy_us", "lead_us", "release_us"):
+            r[k] = round(r[k] / R, 1)
+    res = {"rank": rank, "tp": n, "model": model, "batch": B, "prompt_len": plen, "launches": L,
+           "step_us": round(sorted(step_us)[len(step_us) // 2], 1), "per_name": per}
+    if n > 1:
+        allr = [None] * n
+        dist.all_gather_object(allr, res)
+    else:
+        allr = [res]
+    out = {"kind": "decode_trace", "ranks": allr,
+           "step_us_max_over_ranks": max(r["step_us"] for r in allr)}
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+        if out_path:
+            with open(out_path, "w") as f:
+                json.dump(out, f, indent=1)
+    llm.exit()
+    if n > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return out
+
+
 def bench_tp_gemm(T_dec: int = 8, T_pre: int = 4096, H: int = 4096, I: int = 14336) -> None:
     """Row-parallel GEMM + its collective over the TP group (run under torchrun,
     one process per GPU).  Llama-3-8B down_proj shape: ``x [T, I/tp] @ w[H, I/tp]^T``.
@@ -299,6 +419,10 @@ def main(argv=None) -> None:
     tg.add_argument("--inter", type=int, default=14336)
     s = sub.add_parser("decode-step")
     s.add_argument("model"), s.add_argument("B", type=int), s.add_argument("plen", type=int)
+    t = sub.add_parser("decode-trace", help="per-launch timeline of a graph-replayed decode step (torchrun for TP)")
+    t.add_argument("model"), t.add_argument("B", type=int), t.add_argument("plen", type=int)
+    t.add_argument("--replays", type=int, default=5)
+    t.add_argument("--out", default="", help="also write the JSON here")
     args = ap.parse_args(argv)
     if args.cmd == "gemm":
         if args.sweep_splits:
@@ -309,6 +433,8 @@ def main(argv=None) -> None:
                                         args.bn)))
     elif args.cmd == "tp-gemm":
         bench_tp_gemm(args.tokens_decode, args.tokens_prefill, args.hidden, args.inter)
+    elif args.cmd == "decode-trace":
+        decode_trace(args.model, args.B, args.plen, args.replays, args.out)
     elif args.cmd == "attn-decode":
         print(json.dumps(bench_attn_decode(args.B, args.L, args.Hq, args.Hkv, args.splits)))
     elif args.cmd == "attn-prefill":

@@ -1001,7 +1001,7 @@ void attn_set_trace(torch::Tensor buf) {
 }
 
 int gemm_num_sms();
-unsigned long long* next_span();
+unsigned long long* next_span(const char* name);
 
 // Per-device split-merge counters (zeroed once; the merging CTA re-arms its counter).
 static int* attn_counters(int dev, size_t n) {
@@ -1134,7 +1134,7 @@ void attention(torch::Tensor out, torch::Tensor q, torch::Tensor kv, torch::Tens
     n_counters = (size_t)qt * num_seqs * Hkv;
   }
   p.trace = g_attn_trace;
-  p.span = next_span();
+  p.span = next_span(decode ? "attn_decode" : "attn_prefill");
   torch::Tensor po, pl;
   if (p.num_splits > 1) {
     if (part_o.has_value() && part_o->defined() && part_o->numel() >= (int64_t)T * Hq * p.num_splits * D) {

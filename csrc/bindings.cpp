@@ -22,6 +22,7 @@ void gemm_set_trace(torch::Tensor buf);
 void gemm_force_splits(int64_t n);
 void gemm_force_bn(int64_t n);
 int64_t span_trace(torch::Tensor buf);
+std::vector<std::string> span_names();
 void gemm_allreduce_add(torch::Tensor residual, torch::Tensor x, torch::Tensor w, torch::Tensor peers,
                         int64_t flags_off, int64_t tile_flags_off, int64_t max_tiles, int64_t rank, int64_t tp,
                         int64_t maxT, torch::Tensor epoch_state, torch::Tensor status, double timeout_s);
@@ -83,6 +84,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_set_trace", &braid::gemm_set_trace, "profiling: per-CTA phase timestamps of later GEMMs");
   m.def("span_trace", &braid::span_trace,
         "profiling: record {first CTA start, first dependency-wait exit, last CTA end} of later GEMM/attention launches");
+  m.def("span_names", &braid::span_names, "profiling: names of the launches recorded by span_trace, in order");
   m.def("gemm_force_bn", &braid::gemm_force_bn, "tuning: force the decode token-tile width (0 = heuristic)");
   m.def("gemm_force_splits", &braid::gemm_force_splits, "tuning: force the split-K factor (0 = heuristic)");
   m.def("gemm_check_error", &braid::gemm_check_error, "read and clear the GEMM bounded-wait error flag");

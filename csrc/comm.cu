@@ -29,7 +29,11 @@
 #include "common.cuh"
 #include "launch.cuh"
 
+#include <tuple>
+
 namespace braid {
+
+unsigned long long* next_span(const char* name);
 
 // Layout of one rank's communication buffer (offsets in bytes):
 //   [0, data_bytes)                recv[2][tp][maxT][H] bf16
@@ -70,8 +74,16 @@ __global__ void tp_push_kernel(const __nv_bfloat16* __restrict__ x, int T, int H
 __global__ void tp_reduce_add_kernel(__nv_bfloat16* __restrict__ residual, int T, int H, const char* __restrict__ buf,
                                      int64_t flags_off, int tp, int maxT, int rank, uint64_t arrivals_per_call,
                                      uint64_t* epoch_state, int* status, uint64_t timeout_ns, int add_residual,
-                                     __nv_bfloat16* __restrict__ out) {
+                                     __nv_bfloat16* __restrict__ out, unsigned long long* span) {
   __shared__ int s_fail;
+  if (threadIdx.x == 0) span_start(span);
+  // Programmatic dependent launch: let the next kernel (the consuming GEMM)
+  // launch at once so its weight prefetch overlaps this wait; its own
+  // dependency wait still covers all of this kernel.  The epoch state was last
+  // written by the previous reduce, which the producing GEMM's dependency
+  // chain has completed once this kernel's own dependency wait returns.
+  pdl_trigger();
+  pdl_wait();
   const uint64_t epoch = epoch_state[0];
   const uint64_t expected = epoch_state[1] + arrivals_per_call;
   const int slot = (int)(epoch & 1);
@@ -94,6 +106,7 @@ __global__ void tp_reduce_add_kernel(__nv_bfloat16* __restrict__ residual, int T
     }
   }
   __syncthreads();
+  if (threadIdx.x == 0) span_waited(span);
   if (!s_fail) {
     const __nv_bfloat16* recv = reinterpret_cast<const __nv_bfloat16*>(buf) + (size_t)slot * tp * maxT * H;
     const size_t n = (size_t)T * H;
@@ -125,6 +138,7 @@ __global__ void tp_reduce_add_kernel(__nv_bfloat16* __restrict__ residual, int T
       epoch_state[1] = expected;
       epoch_state[0] = epoch + 1;
     }
+    span_end(span);
   }
 }
 
@@ -285,12 +299,23 @@ void tp_reduce_add(torch::Tensor out, torch::Tensor residual, bool add_residual,
   TORCH_CHECK(T <= maxT, "tp_reduce_add: too many tokens for the communication buffer");
   const at::cuda::CUDAGuard g(out.device());
   const int blocks = std::max(1, std::min(64, (int)(((int64_t)T * H / 8 + 255) / 256)));
-  tp_reduce_add_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<__nv_bfloat16*>(residual.data_ptr()), T, H, reinterpret_cast<const char*>(buf), flags_off,
-      tp, maxT, rank, (uint64_t)arrivals_per_call, reinterpret_cast<uint64_t*>(epoch_state.data_ptr<int64_t>()),
-      status.data_ptr<int>(), (uint64_t)(timeout_s * 1e9), add_residual ? 1 : 0,
-      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  static const bool use_pdl = [] {  // tuning knob: BRAID_REDUCE_PDL=0 launches it as a plain kernel
+    const char* e = getenv("BRAID_REDUCE_PDL");
+    return !(e && e[0] == '0');
+  }();
+  unsigned long long* span = next_span("tp_reduce_add");
+  auto args = std::make_tuple(reinterpret_cast<__nv_bfloat16*>(residual.data_ptr()), T, H,
+                              reinterpret_cast<const char*>(buf), flags_off, (int)tp, (int)maxT, (int)rank,
+                              (uint64_t)arrivals_per_call, reinterpret_cast<uint64_t*>(epoch_state.data_ptr<int64_t>()),
+                              status.data_ptr<int>(), (uint64_t)(timeout_s * 1e9), add_residual ? 1 : 0,
+                              reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), span);
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  if (use_pdl) {
+    std::apply([&](auto... a) { launch_pdl(tp_reduce_add_kernel, dim3(blocks), dim3(256), 0, st, a...); }, args);
+  } else {
+    std::apply([&](auto... a) { tp_reduce_add_kernel<<<blocks, 256, 0, st>>>(a...); }, args);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
 }
 
 // Returns the all-gather arrivals each rank receives from this owner per call (CTAs).

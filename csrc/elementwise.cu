@@ -96,7 +96,9 @@ __global__ void gelu_tanh_kernel(__nv_bfloat16* out, const __nv_bfloat16* x, siz
 }
 
 __global__ void embedding_kernel(__nv_bfloat16* __restrict__ out, const int* __restrict__ ids,
-                                 const __nv_bfloat16* __restrict__ w, int H, int rows, int vocab_start) {
+                                 const __nv_bfloat16* __restrict__ w, int H, int rows, int vocab_start,
+                                 unsigned long long* span) {
+  if (threadIdx.x == 0) span_start(span);
   const int t = blockIdx.x;
   const int id = ids[t] - vocab_start;
   const bool ok = id >= 0 && id < rows;
@@ -105,6 +107,7 @@ __global__ void embedding_kernel(__nv_bfloat16* __restrict__ out, const int* __r
     if (ok) u = *reinterpret_cast<const uint4*>(w + (size_t)id * H + i);
     *reinterpret_cast<uint4*>(out + (size_t)t * H + i) = u;
   }
+  if (threadIdx.x == 0) span_end(span);
 }
 
 // One warp per (token, head).  Heads [0,Hq) are q, [Hq,Hq+Hkv) k, then v.
@@ -213,6 +216,8 @@ void gelu_tanh(torch::Tensor out, torch::Tensor x) {
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+unsigned long long* next_span(const char* name);
+
 void embedding(torch::Tensor out, torch::Tensor ids, torch::Tensor w, int64_t vocab_start) {
   TORCH_CHECK(ids.scalar_type() == at::kInt, "embedding: int32 ids");
   const int T = ids.size(0), H = w.size(1);
@@ -220,7 +225,8 @@ void embedding(torch::Tensor out, torch::Tensor ids, torch::Tensor w, int64_t vo
   if (!T) return;
   const at::cuda::CUDAGuard g(w.device());
   embedding_kernel<<<T, 128, 0, at::cuda::getCurrentCUDAStream()>>>(bpm(out), ids.data_ptr<int>(), bp(w), H,
-                                                                   (int)w.size(0), (int)vocab_start);
+                                                                   (int)w.size(0), (int)vocab_start,
+                                                                   next_span("embedding"));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

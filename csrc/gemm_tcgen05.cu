@@ -32,6 +32,7 @@
 
 #include <atomic>
 #include <mutex>
+#include <string>
 #include <unordered_map>
 #include <vector>
 
@@ -685,18 +686,23 @@ int gemm_num_sms() {
 
 static unsigned long long* g_span_buf = nullptr;
 static int64_t g_span_cap = 0, g_span_seq = 0;
-// Profiling: record the span of every later GEMM / attention launch into
-// consecutive 4 x u64 slots of `buf` (an empty tensor switches it off).
-// Returns the number of slots used since the previous call.
+static std::vector<std::string> g_span_names;
+// Profiling: record the span of every later native launch into consecutive
+// 4 x u64 slots of `buf` (an empty tensor switches it off), with the launch's
+// name kept on the host.  Returns the number of slots used since the previous call.
 int64_t span_trace(torch::Tensor buf) {
   const int64_t used = g_span_seq;
   g_span_buf = buf.defined() && buf.numel() ? reinterpret_cast<unsigned long long*>(buf.data_ptr<int64_t>()) : nullptr;
   g_span_cap = g_span_buf ? buf.numel() / 4 : 0;
   g_span_seq = 0;
+  g_span_names.clear();
   return used;
 }
-unsigned long long* next_span() {
+// Names of the launches recorded since span tracing was last switched on.
+std::vector<std::string> span_names() { return g_span_names; }
+unsigned long long* next_span(const char* name) {
   if (g_span_buf == nullptr || g_span_seq >= g_span_cap) return nullptr;
+  g_span_names.emplace_back(name ? name : "");
   return g_span_buf + 4 * (g_span_seq++);
 }
 
@@ -834,7 +840,8 @@ static int64_t run_gemm(GemmArgs& a, const torch::Tensor& x, const torch::Tensor
     a.err = scratch_for(x.get_device(), 0, 0).err;
     CUtensorMap ta = make_tmap(x.data_ptr(), T, K, x.stride(0), BM);
     CUtensorMap tb = make_tmap(w.data_ptr(), F, K, w.stride(0), BN);
-    a.span = next_span();
+    a.span = next_span(a.epi == 2 ? "gemm_qkv_persistent" : a.epi == 1 ? "gemm_swiglu_persistent"
+                       : a.epi == 4 ? "gemm_rs_persistent" : "gemm_persistent");
     launch_gemm_persistent(ta, tb, a, BN, st);
     return arrivals;
   }
@@ -881,7 +888,8 @@ static int64_t run_gemm(GemmArgs& a, const torch::Tensor& x, const torch::Tensor
   a.counters = sc.counters;
   a.err = sc.err;
   a.trace = g_trace;
-  a.span = next_span();
+  a.span = next_span(a.epi == 2 ? "gemm_qkv" : a.epi == 1 ? "gemm_swiglu" : a.epi == 3 ? "gemm_push"
+                     : a.epi == 4 ? "gemm_rs" : "gemm");
   dim3 grid(m_tiles, n_tiles, splits);
   const void* pa = swap ? w.data_ptr() : x.data_ptr();
   const void* pb = swap ? x.data_ptr() : w.data_ptr();

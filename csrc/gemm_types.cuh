@@ -312,6 +312,6 @@ void launch_gemm_persistent(const CUtensorMap& ta, const CUtensorMap& tb, const 
                             cudaStream_t st);
 int gemm_num_sms();
 // Profiling: the next launch's span slot (4 x u64) when span tracing is on, else nullptr.
-unsigned long long* next_span();
+unsigned long long* next_span(const char* name);
 
 }  // namespace braid

@@ -96,8 +96,9 @@ __global__ void __launch_bounds__(SNT) sample_kernel(int* __restrict__ out, cons
                                                      const int* __restrict__ top_k, const float* __restrict__ top_p,
                                                      const float* __restrict__ min_p,
                                                      const int64_t* __restrict__ seed, const int64_t* __restrict__ step,
-                                                     int all_greedy) {
+                                                     int all_greedy, unsigned long long* span) {
   __shared__ ArgMax ared[SNT / 32];
+  if (threadIdx.x == 0) span_start(span);
   __shared__ float fred[SNT / 32];
   const int row = blockIdx.x;
   const T* x = logits + (size_t)row * ld_row;
@@ -161,8 +162,13 @@ __global__ void __launch_bounds__(SNT) sample_kernel(int* __restrict__ out, cons
     }
   }
   a = block_argmax(a, ared);
-  if (threadIdx.x == 0) out[row] = a.i;
+  if (threadIdx.x == 0) {
+    out[row] = a.i;
+    span_end(span);
+  }
 }
+
+unsigned long long* next_span(const char* name);
 
 void sample(torch::Tensor out, torch::Tensor logits, torch::Tensor temperature, torch::Tensor top_k,
             torch::Tensor top_p, torch::Tensor min_p, torch::Tensor seed, torch::Tensor step, bool all_greedy) {
@@ -171,16 +177,18 @@ void sample(torch::Tensor out, torch::Tensor logits, torch::Tensor temperature, 
   if (!B) return;
   const at::cuda::CUDAGuard g(logits.device());
   auto st = at::cuda::getCurrentCUDAStream();
+  unsigned long long* span = next_span("sample");
   if (logits.scalar_type() == at::kBFloat16)
     sample_kernel<__nv_bfloat16><<<B, SNT, 0, st>>>(
         out.data_ptr<int>(), reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), V, logits.stride(0),
         temperature.data_ptr<float>(), top_k.data_ptr<int>(), top_p.data_ptr<float>(), min_p.data_ptr<float>(),
-        seed.data_ptr<int64_t>(), step.data_ptr<int64_t>(), all_greedy ? 1 : 0);
+        seed.data_ptr<int64_t>(), step.data_ptr<int64_t>(), all_greedy ? 1 : 0, span);
   else
     sample_kernel<float><<<B, SNT, 0, st>>>(out.data_ptr<int>(), logits.data_ptr<float>(), V, logits.stride(0),
                                             temperature.data_ptr<float>(), top_k.data_ptr<int>(),
                                             top_p.data_ptr<float>(), min_p.data_ptr<float>(),
-                                            seed.data_ptr<int64_t>(), step.data_ptr<int64_t>(), all_greedy ? 1 : 0);
+                                            seed.data_ptr<int64_t>(), step.data_ptr<int64_t>(), all_greedy ? 1 : 0,
+                                            span);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
