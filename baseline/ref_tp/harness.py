@@ -218,13 +218,19 @@ def _decode_requests(llm, prompts, sp, warmup: int, steps: int):
     for p in prompts:
         evs, times = [], []
         with contextlib.redirect_stdout(io.StringIO()):
-            for _ in llm.generate(p, sp, stream=True):
+            for rec in llm.generate(p, sp, stream=True):
+                # The reference yields one record per engine step from the
+                # second step on (the first carries two tokens; the last token
+                # arrives only in the final record): consecutive non-final
+                # records are exactly one decode step apart.
+                if rec.get("finished"):
+                    continue
                 e = torch.cuda.Event(enable_timing=True)
                 e.record()
                 evs.append(e)
                 times.append(time.perf_counter())
         torch.cuda.synchronize()
-        a, b = warmup, warmup + steps  # token records: 0..warmup-1 untimed, then `steps` intervals
+        a, b = warmup, warmup + steps  # records 0..warmup-1 untimed, then `steps` one-step intervals
         if len(evs) <= b:
             raise RuntimeError("reference produced fewer tokens than requested")
         dev_ms += evs[a].elapsed_time(evs[b])
@@ -257,7 +263,7 @@ def _line(args, n, dev_ms, wall, toks, clocks, published, note):
 
 
 def _engine_kwargs(args):
-    max_len = args.prompt_len + args.warmup + args.steps + 64
+    max_len = args.prompt_len + args.warmup + args.steps + 68
     return dict(num_kvcache_blocks=-(-max_len // 256) + 4, max_model_len=max_len, kvcache_block_size=256)
 
 
@@ -273,7 +279,7 @@ def run_tp1(args, clock_sampler, published: float) -> None:
     d = write_checkpoint(os.path.join(tempfile.gettempdir(), f"braid_ref_{args.model}_tp1"), args.model)
     prompts = _prompts(args.batch, args.prompt_len, ARCH[args.model]["vocab_size"])
     llm = LLM(d, **_engine_kwargs(args))
-    sp = SamplingParams(temperature=0.0, max_tokens=args.warmup + args.steps + 1, ignore_eos=True)
+    sp = SamplingParams(temperature=0.0, max_tokens=args.warmup + args.steps + 3, ignore_eos=True)
     with clock_sampler(torch.cuda.current_device()) as clocks:
         e0 = time.time()
         dev_ms, wall, toks = _decode_requests(llm, prompts, sp, args.warmup, args.steps)
@@ -308,7 +314,7 @@ def run_tp(args, clock_sampler, published: float) -> None:
     dist.barrier()
     prompts = _prompts(args.batch, args.prompt_len, ARCH[args.model]["vocab_size"])
     llm = LLM(d, **_engine_kwargs(args))
-    sp = SamplingParams(temperature=0.0, max_tokens=args.warmup + args.steps + 1, ignore_eos=True)
+    sp = SamplingParams(temperature=0.0, max_tokens=args.warmup + args.steps + 3, ignore_eos=True)
     dist.barrier()
     torch.cuda.synchronize()
     with clock_sampler(0) as clocks:

@@ -234,11 +234,13 @@ def decode_trace(model: str, B: int, plen: int, replays: int = 5, out_path: str 
     runner.graphs.pop(B, None)
     C.span_trace(buf)
     llm.step()  # re-captures the bucket with span slots baked into the launches
-    C.span_trace(torch.empty(0, dtype=torch.int64))
     names = C.span_names()
+    C.span_trace(torch.empty(0, dtype=torch.int64))
     L = runner.graphs[B].launches
     # the capture runs the step twice eagerly before recording it: the graph's slots are the last L
     base = len(names) - L
+    if base < 0:
+        raise RuntimeError(f"{len(names)} traced launches for a {L}-launch step")
     names = names[base:]
     MAXU = -1  # all bits set: the initial value for the atomicMin fields
     steps = []

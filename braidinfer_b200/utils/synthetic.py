@@ -66,11 +66,18 @@ def hf_config(preset: str, **over) -> dict:
 
 
 def hf_state_dict(cfg: dict, seed: int = 0, std: float = 0.02, k_norm_range: Optional[float] = None,
-                  dtype=torch.float32) -> dict:
+                  dtype=torch.float32, norm_jitter: float = 0.0) -> dict:
+    """HF-named tensors; norm weights are 1, or uniform in [1 - j, 1 + j] with
+    ``norm_jitter`` j (exercises the folding of RMSNorm weights into GEMMs)."""
     g = torch.Generator().manual_seed(seed)
 
     def rnd(*shape):
         return (torch.randn(*shape, generator=g) * std).to(dtype)
+
+    def norm_w(n):
+        if norm_jitter <= 0:
+            return torch.ones(n, dtype=dtype)
+        return (1 + (torch.rand(n, generator=g) * 2 - 1) * norm_jitter).to(dtype)
 
     sd = {}
     if cfg["model_type"] == "gpt2":
@@ -101,8 +108,8 @@ def hf_state_dict(cfg: dict, seed: int = 0, std: float = 0.02, k_norm_range: Opt
     sd["model.embed_tokens.weight"] = rnd(V, H)
     for i in range(cfg["num_hidden_layers"]):
         p = f"model.layers.{i}."
-        sd[p + "input_layernorm.weight"] = torch.ones(H, dtype=dtype)
-        sd[p + "post_attention_layernorm.weight"] = torch.ones(H, dtype=dtype)
+        sd[p + "input_layernorm.weight"] = norm_w(H)
+        sd[p + "post_attention_layernorm.weight"] = norm_w(H)
         sd[p + "self_attn.q_proj.weight"] = rnd(nh * D, H)
         sd[p + "self_attn.k_proj.weight"] = rnd(nkv * D, H)
         sd[p + "self_attn.v_proj.weight"] = rnd(nkv * D, H)
@@ -112,7 +119,7 @@ def hf_state_dict(cfg: dict, seed: int = 0, std: float = 0.02, k_norm_range: Opt
             sd[p + "self_attn.v_proj.bias"] = rnd(nkv * D)
         sd[p + "self_attn.o_proj.weight"] = rnd(H, nh * D)
         if cfg["model_type"] == "qwen3":
-            sd[p + "self_attn.q_norm.weight"] = torch.ones(D, dtype=dtype)
+            sd[p + "self_attn.q_norm.weight"] = norm_w(D)
             kn = torch.ones(D, dtype=dtype)
             if k_norm_range is not None:
                 kn = (torch.rand(D, generator=g) * 2 - 1).mul(k_norm_range).to(dtype)
@@ -120,7 +127,7 @@ def hf_state_dict(cfg: dict, seed: int = 0, std: float = 0.02, k_norm_range: Opt
         sd[p + "mlp.gate_proj.weight"] = rnd(I, H)
         sd[p + "mlp.up_proj.weight"] = rnd(I, H)
         sd[p + "mlp.down_proj.weight"] = rnd(H, I)
-    sd["model.norm.weight"] = torch.ones(H, dtype=dtype)
+    sd["model.norm.weight"] = norm_w(H)
     if not cfg.get("tie_word_embeddings", False):
         sd["lm_head.weight"] = rnd(V, H)
     return sd
@@ -156,7 +163,7 @@ def write_tokenizer(path: str, vocab_size: int, chat_template: bool = False) -> 
 
 def make_checkpoint(path: str, preset: str, seed: int = 0, std: float = 0.02,
                     k_norm_range: Optional[float] = None, write_weights: bool = True,
-                    chat_template: bool = False, dtype=torch.bfloat16, **over) -> str:
+                    chat_template: bool = False, dtype=torch.bfloat16, norm_jitter: float = 0.0, **over) -> str:
     """Create an HF-layout checkpoint directory and return its path."""
     os.makedirs(path, exist_ok=True)
     cfg = hf_config(preset, **over)
@@ -167,6 +174,6 @@ def make_checkpoint(path: str, preset: str, seed: int = 0, std: float = 0.02,
     if write_weights:
         from safetensors.torch import save_file
 
-        sd = hf_state_dict(cfg, seed=seed, std=std, k_norm_range=k_norm_range, dtype=dtype)
+        sd = hf_state_dict(cfg, seed=seed, std=std, k_norm_range=k_norm_range, dtype=dtype, norm_jitter=norm_jitter)
         save_file({k: v.contiguous() for k, v in sd.items()}, os.path.join(path, "model.safetensors"))
     return path
