@@ -178,6 +178,97 @@ def decode_step(model: str, B: int, plen: int) -> None:
     torch.cuda.cudart().cudaProfilerStop()
 
 
+def gemm_trace(M: int, N: int, K: int, kind: str = "plain", rms: bool = True, splits: int = -1,
+               bn: int = 0) -> dict:
+    """Per-CTA phases of one decode-shaped GEMM launch that follows another
+    GEMM in a CUDA graph (so its prologue overlaps a predecessor, as in a
+    decode step).  ``kind``: plain (epi 0), swiglu (epi 1) or qkv (epi 2 with
+    q/k-norm, RoPE and the paged KV append; N = (Hq + 2 Hkv) * 128).
+
+    Per CTA (``gemm_set_trace``): t0 start, t1 MMA issuer ready, t2 first
+    K-block landed, t3 accumulator complete, t4 epilogue done.  Reports the
+    launch span, the medians/maxima of first-data latency, mainloop and
+    epilogue, and the tail = last epilogue end - last accumulator complete
+    (split-K reduction and epilogue of the tiles' last CTAs)."""
+    import numpy as np
+
+    from .. import ops
+    from ..ops._ext import ext
+
+    C = ext()
+    nc = _copies(N * K * 2)
+    ws = [(torch.randn(N, K, device="cuda") * 0.02).bfloat16() for _ in range(nc)]
+    x = torch.randn(M, K, device="cuda").bfloat16()
+    pre_w = (torch.randn(8192, K, device="cuda") * 0.02).bfloat16()
+    pre_out = torch.empty(M, 8192, device="cuda", dtype=torch.bfloat16)
+    eps = 1e-5 if rms else -1.0
+    if kind == "qkv":
+        D, Hkv = 128, 8
+        Hq = N // D - 2 * Hkv
+        PS = 256
+        kv = torch.zeros(M + 1, 2, Hkv, PS, D, device="cuda", dtype=torch.bfloat16)
+        pos = torch.arange(M, device="cuda", dtype=torch.int32) + 100
+        slots = torch.arange(M, device="cuda", dtype=torch.int32) * PS
+        cos, sin = ops.build_cos_sin(D, 500000.0, 4096, None, torch.device("cuda"))
+        q = torch.empty(M, Hq, D, device="cuda", dtype=torch.bfloat16)
+        out = None
+    else:
+        out = torch.empty(M, N // 2 if kind == "swiglu" else N, device="cuda", dtype=torch.bfloat16)
+
+    def launch(i, traced):
+        C.gemm(pre_out, x, pre_w, None, None, 0, -1.0)
+        if traced:
+            C.gemm_set_trace(buf)
+        w = ws[i % nc]
+        if kind == "qkv":
+            C.gemm_qkv(q, x, w, None, eps, pos, slots, kv, None, None, 1e-6, cos, sin, Hq, Hkv, D, True)
+        else:
+            C.gemm(out, x, w, None, None, 1 if kind == "swiglu" else 0, eps)
+        if traced:
+            C.gemm_set_trace(torch.empty(0, dtype=torch.int64))
+
+    C.gemm_force_splits(splits)
+    C.gemm_force_bn(bn)
+    buf = torch.zeros(8 * 4096, dtype=torch.int64, device="cuda")
+    for i in range(3):
+        launch(i, False)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        launch(0, False)
+    torch.cuda.current_stream().wait_stream(s)
+    with torch.cuda.graph(g):
+        for i in range(4):
+            launch(i, i == 3)
+    rows = []
+    for _ in range(5):
+        buf.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        t = buf.view(-1, 8)[:, :5].cpu().numpy().astype("int64")
+        t = t[t[:, 0] > 0]
+        rows.append(t)
+    C.gemm_force_splits(-1)
+    C.gemm_force_bn(0)
+    t = rows[len(rows) // 2]
+    t0 = t[:, 0].min()
+    first = (t[:, 2] - t[:, 0]) / 1e3
+    main = (t[:, 3] - t[:, 2]) / 1e3
+    epi = (t[:, 4] - t[:, 3]) / 1e3
+    med = lambda a: round(float(np.median(a)), 2)  # noqa: E731
+    return {"kind": kind, "M": M, "N": N, "K": K, "ctas": int(len(t)),
+            "span_us": round((t[:, 4].max() - t0) / 1e3, 2),
+            "last_start_us": round((t[:, 0].max() - t0) / 1e3, 2),
+            "first_data_us": {"median": med(first), "max": round(float(first.max()), 2)},
+            "mainloop_us": {"median": med(main), "max": round(float(main.max()), 2)},
+            "epilogue_us": {"median": med(epi), "max": round(float(epi.max()), 2)},
+            "last_acc_us": round((t[:, 3].max() - t0) / 1e3, 2),
+            "tail_us": round((t[:, 4].max() - t[:, 3].max()) / 1e3, 2),
+            "weight_MB": round(N * K * 2 / 1e6, 1)}
+
+
 def decode_trace(model: str, B: int, plen: int, replays: int = 5, out_path: str = "") -> dict:
     """Per-launch timeline of one graph-replayed decode step (one GPU, or every
     rank under torchrun with ``tensor_parallel_size`` = world size).
@@ -236,11 +327,12 @@ def decode_trace(model: str, B: int, plen: int, replays: int = 5, out_path: str 
     llm.step()  # re-captures the bucket with span slots baked into the launches
     names = C.span_names()
     C.span_trace(torch.empty(0, dtype=torch.int64))
-    L = runner.graphs[B].launches
-    # the capture runs the step twice eagerly before recording it: the graph's slots are the last L
-    base = len(names) - L
-    if base < 0:
-        raise RuntimeError(f"{len(names)} traced launches for a {L}-launch step")
+    # the capture runs the step twice eagerly before recording it: three equal
+    # runs of traced launches, the graph's are the last third
+    if len(names) % 3 or not names:
+        raise RuntimeError(f"{len(names)} traced launches is not three equal runs")
+    L = len(names) // 3
+    base = 2 * L
     names = names[base:]
     MAXU = -1  # all bits set: the initial value for the atomicMin fields
     steps = []
@@ -421,6 +513,12 @@ def main(argv=None) -> None:
     tg.add_argument("--inter", type=int, default=14336)
     s = sub.add_parser("decode-step")
     s.add_argument("model"), s.add_argument("B", type=int), s.add_argument("plen", type=int)
+    gt = sub.add_parser("gemm-trace", help="per-CTA phases of a decode GEMM after a predecessor GEMM")
+    gt.add_argument("M", type=int), gt.add_argument("N", type=int), gt.add_argument("K", type=int)
+    gt.add_argument("--kind", default="plain", choices=["plain", "swiglu", "qkv"])
+    gt.add_argument("--no-rms", action="store_true")
+    gt.add_argument("--splits", type=int, default=-1)
+    gt.add_argument("--bn", type=int, default=0)
     t = sub.add_parser("decode-trace", help="per-launch timeline of a graph-replayed decode step (torchrun for TP)")
     t.add_argument("model"), t.add_argument("B", type=int), t.add_argument("plen", type=int)
     t.add_argument("--replays", type=int, default=5)
@@ -435,6 +533,8 @@ def main(argv=None) -> None:
                                         args.bn)))
     elif args.cmd == "tp-gemm":
         bench_tp_gemm(args.tokens_decode, args.tokens_prefill, args.hidden, args.inter)
+    elif args.cmd == "gemm-trace":
+        print(json.dumps(gemm_trace(args.M, args.N, args.K, args.kind, not args.no_rms, args.splits, args.bn)))
     elif args.cmd == "decode-trace":
         decode_trace(args.model, args.B, args.plen, args.replays, args.out)
     elif args.cmd == "attn-decode":

@@ -107,7 +107,10 @@ __global__ void __launch_bounds__(SNT) sample_kernel(int* __restrict__ out, cons
     ArgMax a{-INFINITY, 0x7fffffff};
     for (int i = threadIdx.x; i < V; i += SNT) a = better(a, ArgMax{ld(x, i), i});
     a = block_argmax(a, ared);
-    if (threadIdx.x == 0) out[row] = a.i;
+    if (threadIdx.x == 0) {
+      out[row] = a.i;
+      span_end(span);
+    }
     return;
   }
   const float inv_t = 1.f / fmaxf(temp, 1e-10f);
