@@ -45,7 +45,9 @@ def parse():
                          "chunk under concurrent queries (Llama-3-70B TP8 config)")
     ap.add_argument("--ctx-len", type=int, default=8192, help="cascade: shared context chunk tokens")
     ap.add_argument("--query-len", type=int, default=256, help="cascade: tokens per query")
-    return ap.parse_args()
+    a = ap.parse_args()
+    a.model_given = any(x == "--model" or x.startswith("--model=") for x in sys.argv[1:])
+    return a
 
 
 class ClockSampler:
@@ -266,7 +268,8 @@ def run_cascade(args) -> None:
 
     n = args.gpus
     rank = init_dist(n)
-    model = args.model if args.model != "llama3-8b" else "llama3-70b"
+    # the configuration names Llama-3-70B at TP8; --model picks another architecture
+    model = args.model if args.model_given else "llama3-70b"
     cfg_dir = make_config_dir(model, with_weights=False, rank=rank)
     if n > 1:
         dist.barrier()
@@ -363,7 +366,7 @@ def run_ttft(args) -> None:
     sys.path.insert(0, ROOT)
     from braidinfer_b200 import LLM, ChunkedLLM, ChunkType, SamplingParams
 
-    model = args.model if args.model != "llama3-8b" else "tinyllama-1.1b"
+    model = args.model if args.model_given else "tinyllama-1.1b"
     d = make_config_dir(model, with_weights=False)
     cl = ChunkedLLM(d, load_weights=False, num_kvcache_blocks=400, kvcache_block_size=256, max_model_len=8192,
                     max_num_batched_tokens=32768, max_graph_batch=8)

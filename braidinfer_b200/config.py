@@ -139,7 +139,7 @@ class Config:
     max_prefill_graph_tokens: int = 256  # single-sequence prefills up to this many tokens replay a graph
     comm_backend: str = "fused"   # "fused" (in-kernel peer stores) | "nccl" (baseline)
     comm_timeout_s: float = 5.0
-    heartbeat_every: int = 0       # TP: check peer liveness every N engine steps (0 = off)
+    heartbeat_every: int = 64      # TP: check peer liveness every N engine steps (0 = off)
     seed: int = 0
     load_weights: bool = True     # False: random-init weights (synthetic benchmarks)
     init_std: float = 0.02

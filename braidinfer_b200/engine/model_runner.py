@@ -81,7 +81,12 @@ class ModelRunner:
         log.info("model ready in %.1fs", time.time() - t0)
         self.page_manager: Optional[PageManager] = None
         self.page_size = config.kvcache_block_size
+        # decode graphs per batch bucket; under tensor parallelism with the
+        # peer-memory runtime these sample through the record exchange, and
+        # steps whose settings need the full distribution replay the
+        # logits-all-gather variant (graphs_gather)
         self.graphs: Dict[int, _GraphSlot] = {}
+        self.graphs_gather: Dict[int, _GraphSlot] = {}
         self.sms = _num_sms(self.device)
         self.timing = {"steps": 0, "prefill_tokens": 0, "decode_tokens": 0}
         self.capture_logits: Optional[list] = None  # debug/test hook (eager steps only)
@@ -255,9 +260,18 @@ class ModelRunner:
         pages_per_seq = -(-self.config.max_model_len // self.page_size) + max_segs
         return B * max_segs, B * pages_per_seq
 
-    def _capture(self, B: int, prefill_tokens: int = 0) -> _GraphSlot:
+    def _tp_sampling(self, seqs: List[Sequence]) -> bool:
+        """True when this step samples through the vocab-parallel record
+        exchange (TP with the peer-memory runtime, every row's settings exact there)."""
+        fc = self.fused_comm
+        if fc is None or self.tp.size == 1 or not hasattr(self.model, "sample_tp"):
+            return False
+        return all(fc.can_sample(s.temperature, s.top_k, s.top_p, s.min_p) for s in seqs)
+
+    def _capture(self, B: int, prefill_tokens: int = 0, tp_sampling: bool = False) -> _GraphSlot:
         """Capture one engine step: a decode step of ``B`` sequences, or (with
-        ``prefill_tokens``) a prefill of one sequence padded to that many tokens."""
+        ``prefill_tokens``) a prefill of one sequence padded to that many tokens.
+        ``tp_sampling``: sample through the vocab-parallel record exchange."""
         g = _GraphSlot()
         g.seg_cap, g.page_cap = self._graph_caps(B)
         pm = self.page_manager
@@ -289,8 +303,11 @@ class ModelRunner:
             if prefill_tokens:
                 h = h.index_select(0, views["logits_idx"].long())
             hn = self.model.final_hidden(h)
-            logits = self.model.compute_logits(hn)
-            ops.sample(logits, g.fbuf[0], g.ibuf, g.fbuf[1], g.fbuf[2], g.lbuf[0], g.lbuf[1], out=g.out)
+            if tp_sampling:
+                self.model.sample_tp(hn, g.fbuf[0], g.ibuf, g.fbuf[1], g.fbuf[2], g.lbuf[0], g.lbuf[1], g.out)
+            else:
+                logits = self.model.compute_logits(hn)
+                ops.sample(logits, g.fbuf[0], g.ibuf, g.fbuf[1], g.fbuf[2], g.lbuf[0], g.lbuf[1], out=g.out)
 
         s = torch.cuda.Stream(self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
@@ -318,17 +335,23 @@ class ModelRunner:
 
     def capture_all(self, max_batch: Optional[int] = None) -> None:
         mb = min(max_batch or self.config.max_graph_batch, self.config.max_graph_batch)
+        tps = self.fused_comm is not None and self.tp.size > 1 and hasattr(self.model, "sample_tp")
         for b in sorted(GRAPH_BUCKETS, reverse=True):
             if b <= mb and b not in self.graphs:
-                self.graphs[b] = self._capture(b)
+                self.graphs[b] = self._capture(b, tp_sampling=tps)
 
     def _run_graph(self, seqs: List[Sequence]) -> Optional[List[int]]:
         B = self._bucket(len(seqs))
         if B < 0:
             return None
-        g = self.graphs.get(B)
+        tps = self._tp_sampling(seqs)
+        if not tps and self.fused_comm is not None and self.tp.size > 1 and hasattr(self.model, "sample_tp"):
+            table = self.graphs_gather  # settings that need the whole distribution
+        else:
+            table = self.graphs
+        g = table.get(B)
         if g is None:
-            g = self.graphs[B] = self._capture(B)
+            g = table[B] = self._capture(B, tp_sampling=tps)
         try:
             plan = build_plan(self._items_for(seqs), self.page_size, pad_seqs=B - len(seqs),
                               scratch_page=self.page_manager.scratch_page, seg_cap=g.seg_cap, page_cap=g.page_cap)

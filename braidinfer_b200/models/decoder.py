@@ -24,6 +24,7 @@ GEMM + residual.  The final norm is folded into a copy of the LM head.
 from __future__ import annotations
 
 import math
+import os
 from typing import Dict, Optional
 
 import torch
@@ -33,6 +34,8 @@ from ..config import ModelSpec
 from ..parallel import comm
 from ..parallel.layout import TPLayout
 from ..parallel.state import TPState
+
+PREFETCH_ALL = os.environ.get("BRAID_PREFETCH_ALL", "0") == "1"
 
 
 class LayerWeights:
@@ -243,14 +246,25 @@ class DecoderLM:
         fc = comm.get_fused_comm() if self.tp.size > 1 else None
         if fc is not None and input_ids.is_cuda and fc.can_sp(input_ids.shape[0]):
             return self._forward_sp(fc, input_ids, positions, slot_mapping, meta, kv_cache, workspace)
+        # Decode under tensor parallelism: the reduce kernel that waits for the
+        # peers' partials pulls leading K-blocks of the next GEMM's weight into
+        # L2 meanwhile (HBM is idle then).  BRAID_PREFETCH_ALL=1 makes every
+        # launch prefetch the following GEMM's weight too (measured slower on
+        # B200 at TP1/TP2: the extra traffic competes with the running kernel).
+        T = input_ids.shape[0]
+        nxt = ops.prefetch_next if PREFETCH_ALL else (lambda w, t, skip=0: skip)
         residual = self.embed_tokens(input_ids, positions)
         for i, w in enumerate(self.layers):
+            following = self.layers[i + 1].qkv_w if i + 1 < len(self.layers) else self.lm_head_folded
+            nxt(w.o_w, T)
             q = ops.qkv_gemm(residual, w.qkv_w, w.qkv_b, eps, positions, slot_mapping, kv_cache[i], L.q_heads,
                              L.kv_heads, S.head_dim, self.cos, self.sin, w.q_norm, w.k_norm, eps, S.use_rope)
+            gu_done = nxt(w.gu_w, T)
             o = ops.attention(q, kv_cache[i], meta, self.cos, self.sin, self.scale, S.use_rope, workspace)
-            residual = self._row_parallel(o, w.o_w, residual)
+            residual = self._row_parallel(o, w.o_w, residual, w.gu_w, gu_done)
+            nxt(w.down_w, T)
             g = ops.linear_swiglu(residual, w.gu_w, rms_eps=eps)
-            residual = self._row_parallel(g, w.down_w, residual)
+            residual = self._row_parallel(g, w.down_w, residual, following)
         return residual
 
     def _forward_sp(self, fc, input_ids, positions, slot_mapping, meta, kv_cache, workspace) -> torch.Tensor:
@@ -282,18 +296,32 @@ class DecoderLM:
         fc.sp_wait()
         return G.clone()
 
-    def _row_parallel(self, x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor) -> torch.Tensor:
-        """``residual += x @ w.T`` summed over tensor-parallel ranks."""
+    def _row_parallel(self, x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor,
+                      w_next: Optional[torch.Tensor] = None, skip: int = 0) -> torch.Tensor:
+        """``residual += x @ w.T`` summed over tensor-parallel ranks; the
+        GEMM (and the reduce kernel after it) prefetch ``w_next`` into L2,
+        past the ``skip`` leading K-blocks per slice already requested."""
+        T = x.shape[0]
+        done = ops.prefetch_next(w_next, T, skip) if PREFETCH_ALL else skip
         if self.tp.size == 1:
             return ops.linear(x, w, residual=residual, out=residual)
         fc = comm.get_fused_comm()
         if fc is not None and fc.can_all_reduce(residual):
-            return fc.linear_all_reduce_add(x, w, residual)
+            return fc.linear_all_reduce_add(x, w, residual, w_next, done)
         return comm.all_reduce_add(ops.linear(x, w), residual)
 
     def final_hidden(self, h: torch.Tensor) -> torch.Tensor:
         """Rows fed to the LM head; the final RMSNorm is fused into ``compute_logits``."""
         return h
+
+    def sample_tp(self, h: torch.Tensor, temperature, top_k, top_p, min_p, seed, step, out: torch.Tensor):
+        """Tensor parallelism: LM head on this rank's vocab shard (final norm
+        folded in), then the sampler exchange over peer memory — no logits
+        all-gather.  Returns ``out`` (one token per row, same on every rank)."""
+        fc = comm.get_fused_comm()
+        local = ops.linear(h, self.lm_head_folded, rms_eps=self.spec.rms_norm_eps)
+        return fc.sample(local, self.layout.vocab_start, self.spec.vocab_size, temperature, top_k, top_p, min_p,
+                         seed, step, out)
 
     def compute_logits(self, h: torch.Tensor) -> torch.Tensor:
         """Full-vocabulary logits ``[B, V]`` from residual-stream rows ``h``."""

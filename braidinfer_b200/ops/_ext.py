@@ -13,9 +13,14 @@ from ..errors import KernelUnavailableError
 _C = None
 _err: Exception | None = None
 
-# Number of native kernel launches issued through ``ext()`` (each binding
-# launches one kernel; ops that launch more add the difference via ``count``).
+# Number of native kernel launches issued through ``ext()`` (each kernel
+# binding launches one kernel; ops that launch more add the difference via
+# ``count``).  Bindings that launch nothing are not counted.
 launches = 0
+_NOT_LAUNCHES = frozenset({
+    "span_trace", "span_names", "gemm_set_trace", "attn_set_trace", "gemm_force_bn", "gemm_force_splits",
+    "gemm_check_error", "gemm_prefetch_next", "comm_alloc", "comm_open", "comm_close", "comm_free",
+    "comm_tensor", "tp_sample_record_bytes"})
 
 
 class _Counted:
@@ -24,7 +29,7 @@ class _Counted:
 
     def __getattr__(self, name):
         fn = getattr(self._mod, name)
-        if not callable(fn):
+        if not callable(fn) or name in _NOT_LAUNCHES:
             return fn
 
         def call(*a, **kw):

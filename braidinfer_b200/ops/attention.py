@@ -166,9 +166,6 @@ def attention(q: torch.Tensor, kv_layer: torch.Tensor, meta: AttnMeta, cos: torc
         T, Hq, D = q.shape
         out = torch.empty(T, Hq * D, dtype=q.dtype, device=q.device)
         ws = workspace or {}
-        if meta.decode and meta.num_splits > 1:
-            from . import _ext
-            _ext.count(1)  # split-KV merge kernel
         ext().attention(out, q, kv_layer, meta.qo_indptr, meta.positions, meta.seg_indptr,
                         meta.seg_page_indptr, meta.seg_offset, meta.seg_len, meta.seg_pos0, meta.seg_delta,
                         meta.page_ids, cos, sin, float(scale), bool(use_rope), int(meta.num_seqs),

@@ -65,6 +65,18 @@ def linear(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None
     return y
 
 
+def prefetch_next(w: Optional[torch.Tensor], tokens: int, skip: int = 0) -> int:
+    """Name the weight of a later decode GEMM: the NEXT native launch pulls
+    K-blocks ``[skip, skip + depth)`` of every K-slice of ``w`` into L2 once
+    its own loads are issued (``gemm_prefetch_next``), so the weight stream
+    continues across kernel boundaries.  Returns ``skip + depth`` (the blocks
+    of each slice now requested).  No-op on CPU, for ``None`` and for
+    prefill-sized ``tokens`` (> 64)."""
+    if w is not None and w.is_cuda and tokens <= 64:
+        return skip + int(ext().gemm_prefetch_next(w, int(tokens), int(skip)))
+    return skip
+
+
 def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor, block: int = SWIGLU_BLOCK) -> torch.Tensor:
     """``[I, K] x2 -> [2*I_pad, K]`` with zero-padded ``I_pad = ceil(I/block)*block``."""
     I, K = gate.shape

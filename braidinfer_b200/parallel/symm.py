@@ -83,6 +83,12 @@ class FusedComm:
         off += align(self.sp_max * 4)
         self.recv_off = off
         off += align(tp.size * (-(-self.sp_max // tp.size)) * hidden * 2)
+        # vocab-parallel sampling: per-row records [2 slots][tp][max_tokens] + per-source counters
+        self.rec_bytes = int(self._C.tp_sample_record_bytes())
+        self.sample_recv_off = off
+        off += align(2 * tp.size * max_tokens * self.rec_bytes)
+        self.sample_flags_off = off
+        off += align(8 * tp.size)
         nbytes = off + 256
         self.sp_rs_expected = 0
         self.sp_ag_expected = 0
@@ -102,6 +108,7 @@ class FusedComm:
         self.peers = torch.tensor(self.peer_ptrs, dtype=torch.int64, device=device)
         # [0] epoch (completed calls), [1] cumulative expected arrivals, [2] CTA done counter
         self.epoch_state = torch.zeros(4, dtype=torch.int64, device=device)
+        self.sample_state = torch.zeros(4, dtype=torch.int64, device=device)  # sampler calls, expected, rows done
         self.status = torch.zeros(4, dtype=torch.int32, device=device)
         self.push_fault = False  # test hook: skip the push (a peer that never signals)
         import os
@@ -119,7 +126,8 @@ class FusedComm:
         st = self.status.tolist()
         if st[0] != 0:
             self.status.zero_()
-            what = {1: "all-reduce", 2: "all-gather", 3: "reduce-scatter"}.get(st[0], "collective")
+            what = {1: "all-reduce", 2: "all-gather", 3: "reduce-scatter", 4: "sampler exchange"}.get(st[0],
+                                                                                                  "collective")
             raise CommTimeoutError(
                 f"rank {st[1]} timed out after {self.timeout_s}s waiting for rank {st[2]} ({what} #{st[3]})",
                 {"code": st[0], "rank": st[1], "peer": st[2], "epoch": st[3]})
@@ -187,7 +195,8 @@ class FusedComm:
                             self.epoch_state)
         return self._reduce(residual, residual, self._push_arrivals(partial))
 
-    def linear_all_reduce_add(self, x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor) -> torch.Tensor:
+    def linear_all_reduce_add(self, x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor,
+                              w_next: Optional[torch.Tensor] = None, skip: int = 0) -> torch.Tensor:
         """``residual += sum_ranks(x @ w.T)`` in ONE kernel: each 128-feature tile
         is pushed to every peer from the GEMM epilogue, the tile's CTA waits for
         the peers' copies of the same tile and reduces them with the residual.
@@ -200,7 +209,29 @@ class FusedComm:
             return residual
         arrivals = self._C.gemm_push(x, w, self.peers, self.flags_off, self.tp.rank, self.tp.size, self.maxT,
                                      self.epoch_state)
+        if w_next is not None and x.shape[0] <= 64:  # the reduce kernel prefetches further while it waits
+            self._C.gemm_prefetch_next(w_next, x.shape[0], skip)
         return self._reduce(residual, residual, arrivals)
+
+    # --------------------------------------------------------- sampling
+    TP_SAMPLE_MAX_TOP_K = 32  # candidates per rank and row in the sampler records
+
+    def can_sample(self, temperature: float, top_k: int, top_p: float, min_p: float) -> bool:
+        """Settings the record exchange samples exactly (else: logits all-gather)."""
+        if temperature <= 0:
+            return True
+        if top_k <= 0:
+            return top_p >= 1.0 and min_p <= 0.0
+        return top_k <= self.TP_SAMPLE_MAX_TOP_K
+
+    def sample(self, local_logits: torch.Tensor, vocab_start: int, vocab_size: int, temperature, top_k, top_p,
+               min_p, seed, step, out: torch.Tensor) -> torch.Tensor:
+        """Token per row from this rank's vocab shard of the logits: per-shard
+        records are exchanged over peer memory and merged on every rank."""
+        self._C.tp_sample(out, local_logits, int(vocab_start), int(vocab_size), temperature, top_k, top_p, min_p,
+                          seed, step, self.peers, self.sample_recv_off, self.sample_flags_off, self.tp.rank,
+                          self.tp.size, self.maxT, self.sample_state, self.status, self.timeout_s)
+        return out
 
     def all_reduce_add_rms_norm(self, partial, residual, w, eps, out=None):
         from ..ops.norm import rms_norm

@@ -63,6 +63,8 @@ struct AttnParams {
   int* counters;    // [T * Hkv] split arrival counters, kept at zero between launches
   unsigned long long* trace;  // optional per-CTA phase timestamps (profiling)
   unsigned long long* span;   // optional launch span (profiling)
+  PrefetchArgs pf;            // decode: the next GEMM's weight to pull into L2 (tensor map tmP)
+  int kv_evict_first;         // decode: read K/V with the evict-first L2 policy
 };
 
 constexpr float LOG2E = 1.4426950408889634f;
@@ -273,7 +275,8 @@ BRAID_DEVICE void pc_next(const AttnParams& p, ProdCursor& c, int r0, int r1) {
 // slot space; keys outside the segment or the split range are masked.
 template <int D, int STAGES, int BR>
 __global__ void __launch_bounds__(128, 2) attn_decode_kernel(const __grid_constant__ CUtensorMap tmkv,
-                                                             const AttnParams p) {
+                                                             const AttnParams p,
+                                                             const __grid_constant__ CUtensorMap tmP) {
   constexpr int TILE = KT * D * 2;  // bytes of one K (or V) tile
   extern __shared__ uint8_t sm_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
@@ -329,8 +332,16 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(const __grid_consta
         const int row_v = row_k + p.Hkv * p.PS;
 #pragma unroll
         for (int h = 0; h < D / 64; ++h) {
-          tma_load_2d(kbuf + st * TILE + h * (KT * 128) + q * BR * 128, &tmkv, &full[st], h * 64, row_k);
-          tma_load_2d(vbuf + st * TILE + h * (KT * 128) + q * BR * 128, &tmkv, &full[st], h * 64, row_v);
+          uint8_t* dk = kbuf + st * TILE + h * (KT * 128) + q * BR * 128;
+          uint8_t* dv = vbuf + st * TILE + h * (KT * 128) + q * BR * 128;
+          if (p.kv_evict_first) {
+            const uint64_t pol = l2_evict_first_policy();
+            tma_load_2d_hint(dk, &tmkv, &full[st], h * 64, row_k, pol);
+            tma_load_2d_hint(dv, &tmkv, &full[st], h * 64, row_v, pol);
+          } else {
+            tma_load_2d(dk, &tmkv, &full[st], h * 64, row_k);
+            tma_load_2d(dv, &tmkv, &full[st], h * 64, row_v);
+          }
         }
       }
     }
@@ -483,6 +494,9 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(const __grid_consta
 
   // ---- merge the 4 warps' partial states (reuse the K/V buffers)
   __syncthreads();
+  if (threadIdx.x == 0)  // every K/V tile has landed: pull this CTA's share of the next GEMM's weight into L2
+    prefetch_next_weight(&tmP, p.pf, (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x,
+                         gridDim.x * gridDim.y * gridDim.z);
   if (tr != nullptr && threadIdx.x == 0) tr[3] = globaltimer_ns();
   constexpr int AW_LD = D + 4;  // padded rows: no bank conflicts
   float* mw = reinterpret_cast<float*>(kbuf);        // [4][16]
@@ -1002,6 +1016,7 @@ void attn_set_trace(torch::Tensor buf) {
 
 int gemm_num_sms();
 unsigned long long* next_span(const char* name);
+PrefetchArgs take_prefetch(CUtensorMap* map, const CUtensorMap& fallback);
 
 // Per-device split-merge counters (zeroed once; the merging CTA re-arms its counter).
 static int* attn_counters(int dev, size_t n) {
@@ -1036,7 +1051,9 @@ static void launch_attn(AttnParams& p, int num_seqs, int max_q_len, bool decode,
         attr = true;
       }
       CUtensorMap tm = make_tmap(p.kv, rows, D, D, 64);
-      launch_pdl(k, dim3(num_seqs, p.Hkv, p.num_splits), dim3(128), smem, st, tm, p);
+      CUtensorMap tp;
+      p.pf = take_prefetch(&tp, tm);
+      launch_pdl(k, dim3(num_seqs, p.Hkv, p.num_splits), dim3(128), smem, st, tm, p, tp);
     } else {
       auto k = attn_decode_kernel<D, STAGES, 16>;
       static bool attr = false;
@@ -1045,7 +1062,9 @@ static void launch_attn(AttnParams& p, int num_seqs, int max_q_len, bool decode,
         attr = true;
       }
       CUtensorMap tm = make_tmap(p.kv, rows, D, D, 16);
-      launch_pdl(k, dim3(num_seqs, p.Hkv, p.num_splits), dim3(128), smem, st, tm, p);
+      CUtensorMap tp;
+      p.pf = take_prefetch(&tp, tm);
+      launch_pdl(k, dim3(num_seqs, p.Hkv, p.num_splits), dim3(128), smem, st, tm, p, tp);
     }
   } else {
     constexpr int STAGES = D == 128 ? 2 : 3;
@@ -1135,6 +1154,11 @@ void attention(torch::Tensor out, torch::Tensor q, torch::Tensor kv, torch::Tens
   }
   p.trace = g_attn_trace;
   p.span = next_span(decode ? "attn_decode" : "attn_prefill");
+  static const int kv_ef = [] {  // tuning knob: BRAID_KV_EVICT_FIRST=1 streams decode K/V evict-first
+    const char* e = getenv("BRAID_KV_EVICT_FIRST");
+    return e && e[0] == '1' ? 1 : 0;
+  }();
+  p.kv_evict_first = kv_ef;
   torch::Tensor po, pl;
   if (p.num_splits > 1) {
     if (part_o.has_value() && part_o->defined() && part_o->numel() >= (int64_t)T * Hq * p.num_splits * D) {

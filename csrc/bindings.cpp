@@ -22,6 +22,7 @@ void gemm_set_trace(torch::Tensor buf);
 void gemm_force_splits(int64_t n);
 void gemm_force_bn(int64_t n);
 int64_t span_trace(torch::Tensor buf);
+int64_t gemm_prefetch_next(torch::Tensor w, int64_t T, int64_t skip);
 std::vector<std::string> span_names();
 void gemm_allreduce_add(torch::Tensor residual, torch::Tensor x, torch::Tensor w, torch::Tensor peers,
                         int64_t flags_off, int64_t tile_flags_off, int64_t max_tiles, int64_t rank, int64_t tp,
@@ -53,6 +54,12 @@ void qkv_prepare(torch::Tensor q_out, torch::Tensor qkv, torch::Tensor positions
                  torch::Tensor kv, c10::optional<torch::Tensor> q_norm, c10::optional<torch::Tensor> k_norm,
                  double eps, torch::Tensor cos, torch::Tensor sin, int64_t Hq, int64_t Hkv, int64_t D,
                  bool use_rope);
+int64_t tp_sample_record_bytes();
+void tp_sample(torch::Tensor out, torch::Tensor logits, int64_t vocab_start, int64_t vocab_size,
+               torch::Tensor temperature, torch::Tensor top_k, torch::Tensor top_p, torch::Tensor min_p,
+               torch::Tensor seed, torch::Tensor step, torch::Tensor peers, int64_t recv_off, int64_t flags_off,
+               int64_t rank, int64_t tp, int64_t maxB, torch::Tensor epoch_state, torch::Tensor status,
+               double timeout_s);
 void sample(torch::Tensor out, torch::Tensor logits, torch::Tensor temperature, torch::Tensor top_k,
             torch::Tensor top_p, torch::Tensor min_p, torch::Tensor seed, torch::Tensor step, bool all_greedy);
 }  // namespace braid
@@ -84,6 +91,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_set_trace", &braid::gemm_set_trace, "profiling: per-CTA phase timestamps of later GEMMs");
   m.def("span_trace", &braid::span_trace,
         "profiling: record {first CTA start, first dependency-wait exit, last CTA end} of later GEMM/attention launches");
+  m.def("gemm_prefetch_next", &braid::gemm_prefetch_next,
+        "name the weight of a later decode GEMM; the next launch pulls its K-blocks [skip, skip + depth) of every "
+        "K-slice into L2; returns depth", py::arg("w"), py::arg("T"), py::arg("skip") = 0);
   m.def("span_names", &braid::span_names, "profiling: names of the launches recorded by span_trace, in order");
   m.def("gemm_force_bn", &braid::gemm_force_bn, "tuning: force the decode token-tile width (0 = heuristic)");
   m.def("gemm_force_splits", &braid::gemm_force_splits, "tuning: force the split-K factor (0 = heuristic)");
@@ -97,4 +107,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embedding", &braid::embedding);
   m.def("qkv_prepare", &braid::qkv_prepare);
   m.def("sample", &braid::sample);
+  m.def("tp_sample", &braid::tp_sample,
+        "vocab-parallel sampling: per-shard records exchanged over peer memory, merged identically on every rank");
+  m.def("tp_sample_record_bytes", &braid::tp_sample_record_bytes);
 }

@@ -34,6 +34,7 @@
 namespace braid {
 
 unsigned long long* next_span(const char* name);
+PrefetchArgs take_prefetch(CUtensorMap* map, const CUtensorMap& fallback);
 
 // Layout of one rank's communication buffer (offsets in bytes):
 //   [0, data_bytes)                recv[2][tp][maxT][H] bf16
@@ -74,9 +75,14 @@ __global__ void tp_push_kernel(const __nv_bfloat16* __restrict__ x, int T, int H
 __global__ void tp_reduce_add_kernel(__nv_bfloat16* __restrict__ residual, int T, int H, const char* __restrict__ buf,
                                      int64_t flags_off, int tp, int maxT, int rank, uint64_t arrivals_per_call,
                                      uint64_t* epoch_state, int* status, uint64_t timeout_ns, int add_residual,
-                                     __nv_bfloat16* __restrict__ out, unsigned long long* span) {
+                                     __nv_bfloat16* __restrict__ out, unsigned long long* span,
+                                     const __grid_constant__ CUtensorMap tmP, PrefetchArgs pf) {
   __shared__ int s_fail;
-  if (threadIdx.x == 0) span_start(span);
+  if (threadIdx.x == 0) {
+    span_start(span);
+    // while the peers' partials are in flight, pull the next GEMM's weight into L2
+    prefetch_next_weight(&tmP, pf, blockIdx.x, gridDim.x);
+  }
   // Programmatic dependent launch: let the next kernel (the consuming GEMM)
   // launch at once so its weight prefetch overlaps this wait; its own
   // dependency wait still covers all of this kernel.  The epoch state was last
@@ -304,11 +310,14 @@ void tp_reduce_add(torch::Tensor out, torch::Tensor residual, bool add_residual,
     return !(e && e[0] == '0');
   }();
   unsigned long long* span = next_span("tp_reduce_add");
+  CUtensorMap pf_map;
+  CUtensorMap none{};
+  const PrefetchArgs pf = take_prefetch(&pf_map, none);
   auto args = std::make_tuple(reinterpret_cast<__nv_bfloat16*>(residual.data_ptr()), T, H,
                               reinterpret_cast<const char*>(buf), flags_off, (int)tp, (int)maxT, (int)rank,
                               (uint64_t)arrivals_per_call, reinterpret_cast<uint64_t*>(epoch_state.data_ptr<int64_t>()),
                               status.data_ptr<int>(), (uint64_t)(timeout_s * 1e9), add_residual ? 1 : 0,
-                              reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), span);
+                              reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), span, pf_map, pf);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   if (use_pdl) {
     std::apply([&](auto... a) { launch_pdl(tp_reduce_add_kernel, dim3(blocks), dim3(256), 0, st, a...); }, args);

@@ -158,6 +158,56 @@ BRAID_DEVICE void tma_load_2d(void* smem_dst, const void* desc, uint64_t* bar, i
       : "memory");
 }
 
+// L2 cache policy for streams read exactly once (decode weights, this step's
+// K/V): evicted first, so they do not push out lines other kernels prefetched.
+BRAID_DEVICE uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+// 2D tiled load with an L2 cache-policy hint.
+BRAID_DEVICE void tma_load_2d_hint(void* smem_dst, const void* desc, uint64_t* bar, int x, int y, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;"
+      ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(desc)), "r"(smem_u32(bar)), "r"(x), "r"(y),
+        "l"(pol)
+      : "memory");
+}
+// Prefetch one tile of a tensor map into L2 (no shared memory, no completion).
+BRAID_DEVICE void tma_prefetch_l2_2d(const void* desc, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];"
+               ::"l"(reinterpret_cast<uint64_t>(desc)), "r"(x), "r"(y)
+               : "memory");
+}
+
+// Cross-kernel weight prefetch: a decode-step kernel, once its own loads are
+// issued, pulls the first K-blocks of the NEXT GEMM's weight into L2, in the
+// order that GEMM's CTAs will read them (K-slice `split` of 128-row tile `mt`
+// starts at K-block split * kbps).  So the HBM stream does not stall across
+// the kernel boundary (this kernel's tail, the next kernel's ramp).  The tile
+// is the next GEMM's own TMA box (64 columns x 128 rows, its tensor map).
+struct PrefetchArgs {
+  int m_tiles;   // 128-row tiles of the next weight
+  int splits;    // its K-slices
+  int kbps;      // K-blocks per slice
+  int kb_total;  // K-blocks of a row
+  int skip;      // K-blocks of every slice already prefetched by an earlier launch
+  int depth;     // K-blocks of every slice to prefetch after those (0: none)
+};
+// This CTA's share (CTA `cta` of `ncta`) of the prefetch, issued by one thread.
+BRAID_DEVICE void prefetch_next_weight(const void* tmap, const PrefetchArgs& pf, int cta, int ncta) {
+  if (pf.depth <= 0) return;
+  const int per_depth = pf.m_tiles * pf.splits;
+  const int total = per_depth * pf.depth;
+  for (int i = cta; i < total; i += ncta) {
+    const int j = i / per_depth, r = i % per_depth;
+    const int split = r / pf.m_tiles, mt = r % pf.m_tiles;
+    const int kb = split * pf.kbps + pf.skip + j;
+    if (pf.skip + j < pf.kbps && kb < pf.kb_total) tma_prefetch_l2_2d(tmap, kb * 64, mt * 128);
+  }
+}
+
 // ----------------------------------------------------------------- tcgen05
 BRAID_DEVICE void tmem_alloc(uint32_t* smem_dst, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_dst)),

@@ -102,7 +102,8 @@ BRAID_DEVICE bool et_is_epi_last(int tid) { return tid == 191; }
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
                                                                const __grid_constant__ CUtensorMap tmB,
-                                                               const GemmArgs args) {
+                                                               const GemmArgs args,
+                                                               const __grid_constant__ CUtensorMap tmP) {
   using S = GemmSmem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -161,11 +162,18 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
   if (warp == 0) {
     if (lane == 0) {
       // The weight operand does not depend on the preceding kernel: start
-      // streaming it before the dependency wait (swapped mode: A is the weight).
+      // streaming it before the dependency wait (swapped mode: A is the weight,
+      // read once per step, so it is loaded with the evict-first L2 policy).
+      const uint64_t pol = l2_evict_first_policy();
+      auto load_a = [&](void* dst, uint64_t* bar, int kx) {
+        if (args.swap) tma_load_2d_hint(dst, &tmA, bar, kx, m0, pol);
+        else tma_load_2d(dst, &tmA, bar, kx, m0);
+      };
+      if (args.pf.depth > 0) tma_prefetch_desc(&tmP);
       const int pre = args.swap ? min(nkb, STAGES) : 0;
       for (int i = 0; i < pre; ++i) {
         mbar_arrive_expect_tx(&full[i], S::A_BYTES + S::B_BYTES);
-        tma_load_2d(ringA + i * S::A_BYTES, &tmA, &full[i], (kb0 + i) * BK, m0);
+        load_a(ringA + i * S::A_BYTES, &full[i], (kb0 + i) * BK);
       }
       pdl_wait();
       span_waited(args.span);
@@ -180,9 +188,13 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
         }
         mbar_arrive_expect_tx(&full[s], S::A_BYTES + S::B_BYTES);
         const int kx = (kb0 + i) * BK;
-        tma_load_2d(ringA + s * S::A_BYTES, &tmA, &full[s], kx, m0);
+        load_a(ringA + s * S::A_BYTES, &full[s], kx);
         tma_load_2d(ringB + s * S::B_BYTES, &tmB, &full[s], kx, n0);
       }
+      // this CTA's loads are all issued: pull its share of the next GEMM's
+      // first K-blocks into L2 while the grid drains
+      prefetch_next_weight(&tmP, args.pf, (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x,
+                           gridDim.x * gridDim.y * gridDim.z);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -399,21 +411,28 @@ __global__ void __launch_bounds__(192, 2) gemm_tcgen05_kernel(const __grid_const
         const PushEpi& ps = args.push;
         const int slot = (int)(ps.epoch_state[0] & 1);
         const int m = m0 + r;  // feature (swapped mode)
+        // 16 tokens at a time: the tile is staged token-major in shared memory
+        // (bf16), then every thread sends 16-byte runs of 8 features to each
+        // peer (8x fewer NVLink stores than one element per store).
+        constexpr int XS_LD = BM + 8;
+        __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(xch);  // [16][XS_LD]
         for (int c0 = 0; c0 < BN; c0 += 16) {
           float v[16];
           load_cols(c0, v);
-          if (m < args.M) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int t = n0 + c0 + j;
-              if (t < args.N) {
-                const __nv_bfloat16 y = f2bf(v[j]);
-                for (int p = 0; p < ps.tp; ++p)
-                  reinterpret_cast<__nv_bfloat16*>(ps.peers[p])[(((size_t)slot * ps.tp + ps.rank) * ps.maxT + t) *
-                                                                    args.M + m] = y;
-              }
+          for (int j = 0; j < 16; ++j) xs[j * XS_LD + r] = f2bf(v[j]);
+          named_bar_sync(1, 128);
+          for (int q = et; q < 16 * (BM / 8); q += 128) {
+            const int j = q / (BM / 8), c8 = (q % (BM / 8)) * 8;
+            const int t = n0 + c0 + j, mm = m0 + c8;
+            if (t < args.N && mm < args.M) {
+              const uint4 val = *reinterpret_cast<const uint4*>(xs + j * XS_LD + c8);
+              const size_t off = (((size_t)slot * ps.tp + ps.rank) * ps.maxT + t) * args.M + mm;
+              for (int p = 0; p < ps.tp; ++p)
+                *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(ps.peers[p]) + off) = val;
             }
           }
+          named_bar_sync(1, 128);
         }
         __threadfence_system();
         named_bar_sync(1, 128);
@@ -661,7 +680,8 @@ static SplitKScratch& scratch_for(int dev, size_t ws_bytes, size_t n_counters) {
 int* gemm_error_flag(int dev) { return scratch_for(dev, 0, 0).err; }
 
 template <int BN, int STAGES>
-static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, dim3 grid, cudaStream_t st) {
+static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, dim3 grid, cudaStream_t st,
+                   const CUtensorMap& tp) {
   using S = GemmSmem<BN, STAGES>;
   auto kern = gemm_tcgen05_kernel<BN, STAGES>;
   static bool attr = false;
@@ -671,7 +691,7 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs&
     attr = true;
   }
   launch_pdl_cluster(kern, grid, dim3(192), S::TOTAL, st, a.cluster ? dim3(1, 1, a.splits) : dim3(1, 1, 1), ta, tb,
-                     a);
+                     a, tp);
 }
 
 int gemm_num_sms() {
@@ -749,6 +769,126 @@ static void fill_sp(GemmArgs& a, const c10::optional<torch::Tensor>& sp) {
   TORCH_CHECK(p.rows_per_rank > 0 && p.tp > 0, "gemm: bad sp layout");
 }
 
+// Token-tile width of a swapped (decode) GEMM of T tokens: the narrowest
+// tile for <= 32 tokens; for 33-64 tokens several narrow tiles beat one
+// 64-wide tile unless the weight alone fills the machine (measured on B200,
+// HBM-resident weights): the smallest width whose grid fits one wave with at
+// most 32 K-blocks per CTA, else the width (of those fitting one wave) with
+// the fewest K-blocks per CTA.
+static int swapped_bn(int T, int F, int K) {
+  int BN = T <= 16 ? 16 : T <= 32 ? 32 : 64;
+  const int kb_total = (K + BK - 1) / BK;
+  if (T > 32) {
+    const int slots2 = gemm_num_sms() * 2, mt = (F + BM - 1) / BM;
+    auto kb_per_cta = [&](int bn) {
+      const int tiles = mt * ((T + bn - 1) / bn);
+      const int sp = std::max(1, std::min({slots2 / tiles, kb_total / 2, 16, 256 / bn}));
+      return (kb_total + sp - 1) / sp;
+    };
+    int pick = 0;
+    for (int bn : {16, 32}) {
+      if (mt * ((T + bn - 1) / bn) <= slots2 && kb_per_cta(bn) <= 32) {
+        pick = bn;
+        break;
+      }
+    }
+    if (!pick) {
+      int best = 1 << 30;
+      for (int bn : {16, 32, 64})
+        if (mt * ((T + bn - 1) / bn) <= slots2 && kb_per_cta(bn) < best) {
+          best = kb_per_cta(bn);
+          pick = bn;
+        }
+    }
+    if (pick) BN = pick;
+  }
+  if (g_forced_bn == 16 || g_forced_bn == 32 || g_forced_bn == 64) BN = g_forced_bn;
+  return BN;
+}
+
+// Split-K so that one wave of resident CTAs (2 per SM for decode tiles)
+// covers the machine; decode shapes have few output tiles.  The last CTA of a
+// tile sums splits x BM x BN fp32 partials alone; past 256 partial columns
+// that tail outweighs the shorter K loop (measured on B200 over decode and
+// short-prefill shapes: BN 64 is best at 1-4 splits).
+static void split_plan(int tiles, int kb_total, int BN, bool swap, int& splits, int& kbps) {
+  splits = 1;
+  const int slots = gemm_num_sms() * (swap ? 2 : 1);
+  if (tiles < slots) splits = std::max(1, std::min({slots / tiles, kb_total / 2, 16}));
+  splits = std::max(1, std::min(splits, 256 / BN));
+  const int forced = g_forced_splits >= 0 ? g_forced_splits : [] {  // BRAID_GEMM_SPLITS=n forces the factor
+    static const int env = [] {
+      const char* e = getenv("BRAID_GEMM_SPLITS");
+      return e ? atoi(e) : 0;
+    }();
+    return env;
+  }();
+  if (forced > 0) splits = std::max(1, std::min(forced, kb_total));
+  kbps = (kb_total + splits - 1) / splits;
+  splits = (kb_total + kbps - 1) / kbps;
+}
+
+// ---- cross-kernel weight prefetch (see PrefetchArgs in common.cuh)
+// The host names the weight of the GEMM that follows the next launch
+// (gemm_prefetch_next); that launch receives its tensor map and split plan and
+// pulls the leading K-blocks of every K-slice into L2 (BRAID_PREFETCH_MB caps
+// the bytes per boundary, 0 switches it off).
+struct PendingPrefetch {
+  bool set = false;
+  CUtensorMap map;
+  PrefetchArgs pf;
+};
+static PendingPrefetch g_prefetch;
+
+static size_t prefetch_budget() {
+  static const size_t b = [] {
+    const char* e = getenv("BRAID_PREFETCH_MB");
+    return (size_t)(e ? atof(e) : 48.0) << 20;
+  }();
+  return b;
+}
+
+// Returns the K-blocks per slice that the next launch will prefetch after `skip`.
+int64_t gemm_prefetch_next(torch::Tensor w, int64_t T, int64_t skip) {
+  g_prefetch.set = false;
+  if (!w.defined() || !w.is_cuda() || w.dim() != 2 || T < 1 || T > 64 || prefetch_budget() == 0) return 0;
+  TORCH_CHECK(w.scalar_type() == at::kBFloat16 && w.stride(1) == 1, "gemm_prefetch_next: bf16 row-major weight");
+  const int F = w.size(0), K = w.size(1);
+  const int BN = swapped_bn((int)T, F, K);
+  const int m_tiles = (F + BM - 1) / BM, kb_total = (K + BK - 1) / BK;
+  int splits, kbps;
+  split_plan(m_tiles * (((int)T + BN - 1) / BN), kb_total, BN, true, splits, kbps);
+  PrefetchArgs pf;
+  pf.m_tiles = m_tiles;
+  pf.splits = splits;
+  pf.kbps = kbps;
+  pf.kb_total = kb_total;
+  pf.skip = (int)std::max<int64_t>(0, skip);
+  const size_t box = (size_t)BM * BK * 2;
+  const size_t per_depth = (size_t)m_tiles * splits * box;
+  pf.depth = (int)std::min<size_t>(std::max(0, kbps - pf.skip),
+                                   std::max<size_t>(1, prefetch_budget() / per_depth));
+  if (pf.depth <= 0) return 0;
+  g_prefetch.map = make_tmap(w.data_ptr(), F, K, w.stride(0), BM);
+  g_prefetch.pf = pf;
+  g_prefetch.set = true;
+  return pf.depth;
+}
+
+// Consumed by the next launch: its prefetch arguments and tensor map
+// (`fallback` when nothing is pending; depth 0 then disables the prefetch).
+PrefetchArgs take_prefetch(CUtensorMap* map, const CUtensorMap& fallback) {
+  PrefetchArgs pf{};
+  if (g_prefetch.set) {
+    pf = g_prefetch.pf;
+    *map = g_prefetch.map;
+    g_prefetch.set = false;
+  } else {
+    *map = fallback;
+  }
+  return pf;
+}
+
 static int64_t run_gemm(GemmArgs& a, const torch::Tensor& x, const torch::Tensor& w, bool fused_rms) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda(), "gemm: CUDA tensors required");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "gemm: bf16 only");
@@ -770,37 +910,7 @@ static int64_t run_gemm(GemmArgs& a, const torch::Tensor& x, const torch::Tensor
   a.swap = swap;
   int BN, m_tiles, n_tiles;
   if (swap) {
-    BN = T <= 16 ? 16 : T <= 32 ? 32 : 64;
-    if (T > 32) {
-      // 33-64 tokens: several narrow token tiles beat one 64-wide tile unless the
-      // weight alone fills the machine (measured on B200, HBM-resident weights):
-      // the smallest width whose grid fits one wave with at most 32 K-blocks per
-      // CTA, else the width (of those fitting one wave) with the fewest K-blocks
-      // per CTA.
-      const int slots2 = gemm_num_sms() * 2, mt = (F + BM - 1) / BM;
-      auto kb_per_cta = [&](int bn) {
-        const int tiles = mt * ((T + bn - 1) / bn);
-        const int sp = std::max(1, std::min({slots2 / tiles, kb_total / 2, 16, 256 / bn}));
-        return (kb_total + sp - 1) / sp;
-      };
-      int pick = 0;
-      for (int bn : {16, 32}) {
-        if (mt * ((T + bn - 1) / bn) <= slots2 && kb_per_cta(bn) <= 32) {
-          pick = bn;
-          break;
-        }
-      }
-      if (!pick) {
-        int best = 1 << 30;
-        for (int bn : {16, 32, 64})
-          if (mt * ((T + bn - 1) / bn) <= slots2 && kb_per_cta(bn) < best) {
-            best = kb_per_cta(bn);
-            pick = bn;
-          }
-      }
-      if (pick) BN = pick;
-    }
-    if (g_forced_bn == 16 || g_forced_bn == 32 || g_forced_bn == 64) BN = g_forced_bn;
+    BN = swapped_bn(T, F, K);
     a.M = F;
     a.N = T;
     m_tiles = (F + BM - 1) / BM;
@@ -853,25 +963,8 @@ static int64_t run_gemm(GemmArgs& a, const torch::Tensor& x, const torch::Tensor
     a.rs_vec = rstd_tmp.data_ptr<float>();
   }
   if (a.rs_vec != nullptr) a.rs_x = nullptr;
-  // Split-K so that one wave of resident CTAs (2 per SM for decode tiles)
-  // covers the machine; decode shapes have few output tiles.
-  int splits = 1;
-  const int slots = gemm_num_sms() * (swap ? 2 : 1);
-  if (tiles < slots) splits = std::max(1, std::min({slots / tiles, kb_total / 2, 16}));
-  // The last CTA of a tile sums splits x BM x BN fp32 partials alone; past
-  // 256 partial columns that tail outweighs the shorter K loop (measured on
-  // B200 over decode and short-prefill shapes: BN 64 is best at 1-4 splits).
-  splits = std::max(1, std::min(splits, 256 / BN));
-  const int forced = g_forced_splits >= 0 ? g_forced_splits : [] {  // BRAID_GEMM_SPLITS=n forces the factor
-    static const int env = [] {
-      const char* e = getenv("BRAID_GEMM_SPLITS");
-      return e ? atoi(e) : 0;
-    }();
-    return env;
-  }();
-  if (forced > 0) splits = std::max(1, std::min(forced, kb_total));
-  int kbps = (kb_total + splits - 1) / splits;
-  splits = (kb_total + kbps - 1) / kbps;
+  int splits, kbps;
+  split_plan(tiles, kb_total, BN, swap, splits, kbps);
   a.splits = splits;
   a.kb_per_split = kbps;
   // Optional (BRAID_GEMM_CLUSTER=1): up to 16 K-slices reduce through
@@ -897,12 +990,15 @@ static int64_t run_gemm(GemmArgs& a, const torch::Tensor& x, const torch::Tensor
   const int64_t lda = swap ? w.stride(0) : x.stride(0), ldb = swap ? x.stride(0) : w.stride(0);
   CUtensorMap ta = make_tmap(pa, ra, K, lda, BM);
   CUtensorMap tb = make_tmap(pb, rb, K, ldb, BN);
+  CUtensorMap tp;
+  a.pf = take_prefetch(&tp, ta);
+  if (!swap) a.pf.depth = 0;
   switch (BN) {
-    case 16: launch<16, 4>(ta, tb, a, grid, st); break;
-    case 32: launch<32, 4>(ta, tb, a, grid, st); break;
-    case 64: launch<64, 4>(ta, tb, a, grid, st); break;
-    case 128: launch<128, 6>(ta, tb, a, grid, st); break;
-    default: launch<256, 4>(ta, tb, a, grid, st); break;
+    case 16: launch<16, 4>(ta, tb, a, grid, st, tp); break;
+    case 32: launch<32, 4>(ta, tb, a, grid, st, tp); break;
+    case 64: launch<64, 4>(ta, tb, a, grid, st, tp); break;
+    case 128: launch<128, 6>(ta, tb, a, grid, st, tp); break;
+    default: launch<256, 4>(ta, tb, a, grid, st, tp); break;
   }
   return arrivals;
 }
@@ -993,6 +1089,7 @@ void gemm_allreduce_add(torch::Tensor residual, torch::Tensor x, torch::Tensor w
   TORCH_CHECK((w.size(0) + BM - 1) / BM * ((x.size(0) + 15) / 16) <= max_tiles,
               "gemm_allreduce_add: too many output tiles for the flag area");
   TORCH_CHECK(tp >= 1 && tp <= 8, "gemm_allreduce_add: one NVLink domain of at most 8 ranks");
+  TORCH_CHECK(w.size(0) % 8 == 0, "gemm_allreduce_add: output features must be a multiple of 8");
   TORCH_CHECK(residual.is_contiguous() && residual.size(0) == x.size(0) && residual.size(1) == w.size(0));
   GemmArgs a{};
   a.epi = 3;
@@ -1017,6 +1114,7 @@ void gemm_allreduce_add(torch::Tensor residual, torch::Tensor x, torch::Tensor w
 int64_t gemm_push(torch::Tensor x, torch::Tensor w, torch::Tensor peers, int64_t flags_off, int64_t rank, int64_t tp,
                   int64_t maxT, torch::Tensor epoch_state) {
   TORCH_CHECK(x.size(0) <= 64 && x.size(0) <= maxT, "gemm_push: decode shapes only (<= 64 tokens)");
+  TORCH_CHECK(w.size(0) % 8 == 0, "gemm_push: output features must be a multiple of 8 (16-byte peer stores)");
   GemmArgs a{};
   a.epi = 3;
   a.push.peers = reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>());
@@ -1108,7 +1206,7 @@ static cudaError_t launch_plain(int dev, const CUtensorMap& ta, const CUtensorMa
       g_attr_done[dev].fetch_or(bit, std::memory_order_release);
     }
   }
-  kern<<<grid, 192, S::TOTAL, st>>>(ta, tb, a);
+  kern<<<grid, 192, S::TOTAL, st>>>(ta, tb, a, ta);  // a.pf.depth == 0: no prefetch
   return cudaGetLastError();
 }
 

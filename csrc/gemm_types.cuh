@@ -98,6 +98,7 @@ struct GemmArgs {
   SpArgs sp;
   unsigned long long* trace;  // optional per-CTA phase timestamps (profiling)
   unsigned long long* span;   // optional launch span (profiling)
+  PrefetchArgs pf;            // next GEMM's weight to pull into L2 (third tensor map)
 };
 
 constexpr int BM = 128;

@@ -195,4 +195,247 @@ void sample(torch::Tensor out, torch::Tensor logits, torch::Tensor temperature, 
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+
+// ------------------------------------------------------------------------
+// Vocab-parallel sampling under tensor parallelism (one kernel, no NCCL).
+//
+// Each rank holds the logits of its vocabulary shard [B, Vl] (global id =
+// vocab_start + i).  One CTA per row reduces the shard to a fixed-size
+// record, stores it into every peer's receive slot over NVLink, bumps each
+// peer's arrival counter for this rank, waits (bounded) until every source's
+// records of this call have arrived, and merges the tp records.  Every rank
+// merges the same records the same way, so all ranks pick the same token.
+//   greedy rows            record = local (max logit, id); merge = argmax
+//   temperature only       record = local argmax of z + g(id) (the Gumbel-max
+//                          race restricted to the shard); merge = argmax.
+//                          Exact: g depends only on (seed, step, global id).
+//   top-k <= TPS_KC        record = local top-TPS_KC candidates of z and the
+//                          local z max; the global top-k (and every token that
+//                          min-p / top-p keep after it) lies among the tp x
+//                          TPS_KC candidates, so the merge applies min-p,
+//                          top-k, top-p and the Gumbel race exactly there.
+// Other settings (top-p or min-p without top-k, top-k > TPS_KC) need the full
+// distribution: the host routes such steps to the logits all-gather.
+// Replaces the per-row loops of braidinfer/layers/sampler.py:48-81 and the
+// logits all-gather of the tensor-parallel decode step.
+constexpr int TPS_KC = 32;
+struct TpsRec {  // 4-byte words
+  float zmax;    // local max of z (sampled) or of the logit (greedy)
+  float gval;    // winner value of the local race
+  int gid;       // its global token id
+  int ncand;     // candidates stored
+  float cz[TPS_KC];
+  int cid[TPS_KC];
+};
+static_assert(sizeof(TpsRec) % 16 == 0, "TpsRec is moved in 16-byte units");
+
+__global__ void __launch_bounds__(SNT) tp_sample_kernel(
+    int* __restrict__ out, const __nv_bfloat16* __restrict__ logits, int Vl, int ld_row, int vocab_start,
+    int vocab_size, const float* __restrict__ temperature, const int* __restrict__ top_k,
+    const float* __restrict__ top_p, const float* __restrict__ min_p, const int64_t* __restrict__ seed,
+    const int64_t* __restrict__ step, const uint64_t* __restrict__ peers, int64_t recv_off, int64_t flags_off,
+    int rank, int tp, int maxB, uint64_t* epoch_state, int* status, uint64_t timeout_ns, unsigned long long* span) {
+  __shared__ ArgMax ared[SNT / 32];
+  __shared__ float fred[SNT / 32];
+  __shared__ __align__(16) TpsRec rec;
+  __shared__ int s_n, s_fail;
+  __shared__ float s_cz[8 * TPS_KC];
+  __shared__ int s_cid[8 * TPS_KC];
+  if (threadIdx.x == 0) span_start(span);
+  pdl_wait();
+  const int row = blockIdx.x, B = gridDim.x;
+  const uint64_t epoch = epoch_state[0];
+  const uint64_t expected = epoch_state[1] + (uint64_t)B;
+  const int slot = (int)(epoch & 1);
+  const __nv_bfloat16* x = logits + (size_t)row * ld_row;
+  const int nvalid = max(0, min(Vl, vocab_size - vocab_start));
+  const float temp = temperature[row];
+  const int k = top_k[row];
+  const bool greedy = temp <= 0.f;
+  const float inv_t = greedy ? 1.f : 1.f / fmaxf(temp, 1e-10f);
+  if (threadIdx.x == 0) {
+    s_n = 0;
+    s_fail = 0;
+  }
+  // ---- local record
+  float zmax = -INFINITY;
+  for (int i = threadIdx.x; i < nvalid; i += SNT) zmax = fmaxf(zmax, bf2f(x[i]) * inv_t);
+  zmax = block_reduce_max(zmax, fred);
+  ArgMax a{-INFINITY, 0x7fffffff};
+  if (greedy) {
+    for (int i = threadIdx.x; i < nvalid; i += SNT) a = better(a, ArgMax{bf2f(x[i]), vocab_start + i});
+  } else if (k <= 0) {
+    const uint64_t key = mix64((uint64_t)seed[row] ^ mix64((uint64_t)step[row]));
+    for (int i = threadIdx.x; i < nvalid; i += SNT) {
+      const int gid = vocab_start + i;
+      const float u = hash_uniform(key, (uint64_t)gid);
+      a = better(a, ArgMax{bf2f(x[i]) * inv_t - logf(-logf(u)), gid});
+    }
+  }
+  a = block_argmax(a, ared);
+  if (!greedy && k > 0) {
+    // largest threshold with at least TPS_KC local values above it (bisection)
+    const int want = min(TPS_KC, nvalid);
+    float lo = zmax - 100.f, hi = zmax;
+    for (int it = 0; it < 30; ++it) {
+      const float mid = 0.5f * (lo + hi);
+      float c = 0.f;
+      for (int i = threadIdx.x; i < nvalid; i += SNT) c += (bf2f(x[i]) * inv_t >= mid) ? 1.f : 0.f;
+      c = block_reduce_sum(c, fred);
+      if (c >= (float)want) lo = mid; else hi = mid;
+    }
+    for (int i = threadIdx.x; i < nvalid; i += SNT) {
+      const float z = bf2f(x[i]) * inv_t;
+      if (z >= lo) {
+        const int j = atomicAdd(&s_n, 1);
+        if (j < TPS_KC) {
+          rec.cz[j] = z;
+          rec.cid[j] = vocab_start + i;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    rec.zmax = zmax;
+    rec.gval = a.v;
+    rec.gid = a.i;
+    rec.ncand = min(s_n, TPS_KC);
+  }
+  __syncthreads();
+  // ---- push the record to every rank (self included), then count it there
+  constexpr int NV = sizeof(TpsRec) / 16;
+  if (threadIdx.x < NV) {
+    const uint4 v = reinterpret_cast<const uint4*>(&rec)[threadIdx.x];
+    const size_t off = (size_t)recv_off + (((size_t)slot * tp + rank) * maxB + row) * sizeof(TpsRec);
+    for (int p = 0; p < tp; ++p)
+      reinterpret_cast<uint4*>(reinterpret_cast<char*>(peers[p]) + off)[threadIdx.x] = v;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0)
+    for (int p = 0; p < tp; ++p)
+      atomicAdd(reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(peers[p]) + flags_off) + rank, 1ull);
+  // ---- wait for every source's records of this call (bounded)
+  if (threadIdx.x < tp) {
+    const uint64_t* f = reinterpret_cast<const uint64_t*>(reinterpret_cast<const char*>(peers[rank]) + flags_off) +
+                        threadIdx.x;
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire_sys_u64(f) < expected) {
+      if (globaltimer_ns() - t0 > timeout_ns) {
+        if (atomicCAS(status, 0, 4) == 0) {
+          status[1] = rank;
+          status[2] = threadIdx.x;
+          status[3] = (int)epoch;
+        }
+        s_fail = 1;
+        break;
+      }
+      __nanosleep(32);
+    }
+  }
+  __syncthreads();
+  int token = 0;
+  if (!s_fail) {
+    const TpsRec* recs =
+        reinterpret_cast<const TpsRec*>(reinterpret_cast<const char*>(peers[rank]) + recv_off) + (size_t)slot * tp * maxB;
+    if (greedy || k <= 0) {
+      ArgMax b{-INFINITY, 0x7fffffff};
+      if (threadIdx.x < tp) {
+        const TpsRec* r = recs + (size_t)threadIdx.x * maxB + row;
+        b = ArgMax{__ldcv(&r->gval), __ldcv(&r->gid)};
+      }
+      token = block_argmax(b, ared).i;
+    } else {
+      // candidates of every source: thread i holds candidate i
+      float gz = -INFINITY;
+      for (int src = 0; src < tp; ++src) gz = fmaxf(gz, __ldcv(&recs[(size_t)src * maxB + row].zmax));
+      const int ncap = tp * TPS_KC;
+      if (threadIdx.x < ncap) {
+        const int src = threadIdx.x / TPS_KC, j = threadIdx.x % TPS_KC;
+        const TpsRec* r = recs + (size_t)src * maxB + row;
+        const bool ok = j < __ldcv(&r->ncand);
+        s_cz[threadIdx.x] = ok ? __ldcv(&r->cz[j]) : -INFINITY;
+        s_cid[threadIdx.x] = ok ? __ldcv(&r->cid[j]) : 0x7fffffff;
+      }
+      __syncthreads();
+      const bool mine = threadIdx.x < ncap && s_cz[threadIdx.x] != -INFINITY;
+      const float z = mine ? s_cz[threadIdx.x] : -INFINITY;
+      const int id = mine ? s_cid[threadIdx.x] : 0x7fffffff;
+      // order: larger z first, then smaller id
+      int before = 0;
+      if (mine)
+        for (int j = 0; j < ncap; ++j)
+          before += (s_cz[j] > z || (s_cz[j] == z && s_cid[j] < id)) ? 1 : 0;
+      // k-th largest value: the candidate ranked k - 1 publishes it
+      __shared__ float s_kth;
+      if (threadIdx.x == 0) s_kth = -INFINITY;
+      __syncthreads();
+      if (mine && before == k - 1) s_kth = z;
+      __syncthreads();
+      bool keep = mine && z >= s_kth;
+      const float mp = min_p[row];
+      if (mp > 0.f) keep = keep && z >= gz + logf(mp);
+      const float tpp = top_p[row];
+      if (tpp < 1.f) {
+        const float e = keep ? __expf(z - gz) : 0.f;
+        const float tot = block_reduce_sum(e, fred);
+        __shared__ float s_pr[8 * TPS_KC];
+        if (threadIdx.x < ncap) s_pr[threadIdx.x] = keep ? e / tot : -1.f;
+        __syncthreads();
+        // mass of the kept candidates ordered before this one
+        float mass = 0.f;
+        if (keep)
+          for (int j = 0; j < ncap; ++j)
+            if (s_pr[j] >= 0.f && (s_cz[j] > z || (s_cz[j] == z && s_cid[j] < id))) mass += s_pr[j];
+        const bool nuc = keep && mass < tpp;
+        const float thr = -block_reduce_max(nuc ? -(e / tot) : -INFINITY, fred);
+        keep = keep && e / tot >= thr;
+      }
+      ArgMax b{-INFINITY, 0x7fffffff};
+      if (keep) {
+        const uint64_t key = mix64((uint64_t)seed[row] ^ mix64((uint64_t)step[row]));
+        const float u = hash_uniform(key, (uint64_t)id);
+        b = ArgMax{z - logf(-logf(u)), id};
+      }
+      token = block_argmax(b, ared).i;
+    }
+  }
+  if (threadIdx.x == 0) {
+    out[row] = token;
+    // advance the epoch once every row of this call is merged
+    __threadfence();
+    const unsigned long long done = atomicAdd(reinterpret_cast<unsigned long long*>(epoch_state + 2), 1ull);
+    if (done == (unsigned long long)(B - 1)) {
+      epoch_state[2] = 0;
+      epoch_state[1] = expected;
+      epoch_state[0] = epoch + 1;
+    }
+    span_end(span);
+  }
+}
+
+int64_t tp_sample_record_bytes() { return sizeof(TpsRec); }
+
+void tp_sample(torch::Tensor out, torch::Tensor logits, int64_t vocab_start, int64_t vocab_size,
+               torch::Tensor temperature, torch::Tensor top_k, torch::Tensor top_p, torch::Tensor min_p,
+               torch::Tensor seed, torch::Tensor step, torch::Tensor peers, int64_t recv_off, int64_t flags_off,
+               int64_t rank, int64_t tp, int64_t maxB, torch::Tensor epoch_state, torch::Tensor status,
+               double timeout_s) {
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1 && logits.scalar_type() == at::kBFloat16,
+              "tp_sample: bf16 [B, V_local] logits");
+  TORCH_CHECK(tp >= 1 && tp <= 8, "tp_sample: at most 8 ranks");
+  const int B = logits.size(0), Vl = logits.size(1);
+  TORCH_CHECK(B <= maxB, "tp_sample: batch exceeds the receive area");
+  if (!B) return;
+  const at::cuda::CUDAGuard g(logits.device());
+  launch_pdl(tp_sample_kernel, dim3(B), dim3(SNT), 0, at::cuda::getCurrentCUDAStream(), out.data_ptr<int>(),
+             reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), Vl, (int)logits.stride(0), (int)vocab_start,
+             (int)vocab_size, temperature.data_ptr<float>(), top_k.data_ptr<int>(), top_p.data_ptr<float>(),
+             min_p.data_ptr<float>(), seed.data_ptr<int64_t>(), step.data_ptr<int64_t>(),
+             reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>()), recv_off, flags_off, (int)rank, (int)tp,
+             (int)maxB, reinterpret_cast<uint64_t*>(epoch_state.data_ptr<int64_t>()), status.data_ptr<int>(),
+             (uint64_t)(timeout_s * 1e9), next_span("tp_sample"));
+}
+
 }  // namespace braid
