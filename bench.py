@@ -175,7 +175,9 @@ def timed_decode(llm, args, n: int):
     dev_ms = sum(a.elapsed_time(b) for a, b in runner.event_log)
     runner.event_log = None
     if len(llm.scheduler.running) != args.batch:
-        raise RuntimeError("batch shrank during the timed region")
+        raise RuntimeError(f"batch shrank during the timed region: {len(llm.scheduler.running)} running, "
+                           f"{len(llm.scheduler.waiting)} waiting, {llm.scheduler.num_preemptions} preemptions "
+                           f"(max_model_len {llm.config.max_model_len})")
     t = torch.tensor([dev_ms, wall], device="cuda", dtype=torch.float64)
     if n > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)

@@ -20,6 +20,36 @@ from .sequence import SegmentRef
 
 FIELDS = ("input_ids", "positions", "slots", "qo_indptr", "seg_indptr", "seg_page_indptr",
           "seg_offset", "seg_len", "seg_pos0", "seg_delta", "page_ids", "logits_idx")
+# shared-prefix decode plans also carry: the group's token range, its shared
+# segments (appended after every sequence's own), and a per-sequence member flag
+GROUP_FIELDS = ("grp_qo_indptr", "grp_seg_indptr", "seq_nsh")
+
+
+def _seg_key(s: SegmentRef, page_size: int):
+    npg = -(-(s.offset + s.length) // page_size)
+    return (tuple(s.pages[:npg]), s.offset, s.length, s.pos0, s.delta)
+
+
+def find_shared_group(items: List["FwdItem"], page_size: int, min_keys: int = 256):
+    """Decode items that attend to the same cached segments (same pages,
+    offset, length, position and RoPE delta) can share one pass over them.
+    Returns ``(member indices, shared segment keys)`` for the segment set that
+    saves the most key reads (members x shared keys), or ``None`` when no
+    segment of at least ``min_keys`` keys is used by two or more items."""
+    from collections import Counter
+
+    per_item = [{_seg_key(sg, page_size) for sg in it.segments if sg.length > 0} for it in items]
+    cnt = Counter(k for keys in per_item for k in keys)
+    best, best_gain = None, 0
+    for k, c in cnt.items():
+        if c < 2 or k[2] < min_keys:
+            continue
+        members = [i for i, keys in enumerate(per_item) if k in keys]
+        common = set.intersection(*(per_item[i] for i in members))
+        gain = (len(members) - 1) * sum(x[2] for x in common)
+        if gain > best_gain:
+            best, best_gain = (members, common), gain
+    return best
 
 
 @dataclass
@@ -45,18 +75,27 @@ class Plan:
 
 
 def build_plan(items: List[FwdItem], page_size: int, pad_seqs: int = 0, scratch_page: int = 0,
-               seg_cap: Optional[int] = None, page_cap: Optional[int] = None, pad_tokens: int = -1) -> Plan:
+               seg_cap: Optional[int] = None, page_cap: Optional[int] = None, pad_tokens: int = -1,
+               group: Optional[tuple] = None) -> Plan:
     """Flatten ``items`` into the kernel metadata.  ``pad_seqs`` appends dummy
     one-token sequences (CUDA-graph padding) that write to ``scratch_page``;
     ``pad_tokens >= 0`` appends ONE dummy sequence of that many tokens (padding
     of a prefill graph's token count), also confined to ``scratch_page`` and
-    without a logits row."""
+    without a logits row.
+
+    ``group = (n_members, shared keys)`` (decode plans, members first): the
+    first ``n_members`` items skip the segments whose keys are in ``shared``;
+    those segments are appended once after all others and described by
+    ``grp_qo_indptr`` / ``grp_seg_indptr``; ``seq_nsh`` flags the members.
+    ``group = (0, set())`` emits the same arrays for an empty group."""
     ids, pos, slots = [], [], []
     qo, segi = [0], [0]
     spi, soff, slen, spos0, sdelta, pids = [0], [], [], [], [], []
     lidx = []
     max_q = max_kv = 0
-    for it in items:
+    n_members, shared = group if group is not None else (0, set())
+    shared_segs = []
+    for idx, it in enumerate(items):
         n = len(it.tokens)
         t0 = len(ids)
         ids.extend(it.tokens)
@@ -67,6 +106,11 @@ def build_plan(items: List[FwdItem], page_size: int, pad_seqs: int = 0, scratch_
         kv = 0
         for s in it.segments:
             if s.length <= 0:
+                continue
+            if idx < n_members and _seg_key(s, page_size) in shared:
+                if idx == 0:
+                    shared_segs.append(s)
+                kv += s.length
                 continue
             npg = -(-(s.offset + s.length) // page_size)
             pids.extend(s.pages[:npg])
@@ -121,6 +165,19 @@ def build_plan(items: List[FwdItem], page_size: int, pad_seqs: int = 0, scratch_
             sdelta.append(0)
         segi.append(len(slen))
         max_q = max(max_q, pad_tokens)
+    grp = None
+    if group is not None:
+        g0 = len(slen)
+        for sg in shared_segs:
+            npg = -(-(sg.offset + sg.length) // page_size)
+            pids.extend(sg.pages[:npg])
+            spi.append(len(pids))
+            soff.append(sg.offset)
+            slen.append(sg.length)
+            spos0.append(sg.pos0)
+            sdelta.append(sg.delta)
+        grp = {"grp_qo_indptr": [0, n_members if shared_segs else 0], "grp_seg_indptr": [g0, len(slen)],
+               "seq_nsh": [1 if i < n_members and shared_segs else 0 for i in range(len(qo) - 1)]}
     S = len(slen)
     if seg_cap is not None:
         if S > seg_cap:
@@ -140,31 +197,43 @@ def build_plan(items: List[FwdItem], page_size: int, pad_seqs: int = 0, scratch_
         "seg_page_indptr": spi, "seg_offset": soff, "seg_len": slen, "seg_pos0": spos0, "seg_delta": sdelta,
         "page_ids": pids, "logits_idx": lidx,
     }
+    if grp is not None:
+        arrays.update(grp)
     arrays = {k: np.asarray(v, dtype=np.int32) for k, v in arrays.items()}
     sizes = {k: len(v) for k, v in arrays.items()}
     nseq = len(items) + pad_seqs + (1 if pad_tokens >= 0 else 0)
     return Plan(arrays, nseq, len(ids), max_q, max_kv, decode=(max_q == 1 and len(ids) == nseq), sizes=sizes)
 
 
+def _fields(keys) -> tuple:
+    return FIELDS + (GROUP_FIELDS if "seq_nsh" in keys else ())
+
+
 def pack(plan: Plan) -> np.ndarray:
-    return np.concatenate([plan.arrays[k] for k in FIELDS])
+    return np.concatenate([plan.arrays[k] for k in _fields(plan.arrays)])
 
 
 def unpack(buf: torch.Tensor, sizes: dict) -> dict:
     out, o = {}, 0
-    for k in FIELDS:
+    for k in _fields(sizes):
         n = sizes[k]
         out[k] = buf[o:o + n]
         o += n
     return out
 
 
-def make_meta(views: dict, plan: Plan, num_splits: int = 1) -> AttnMeta:
+def make_meta(views: dict, plan: Plan, num_splits: int = 1, shared_splits: int = 0) -> AttnMeta:
     host = None
     if not views["qo_indptr"].is_cuda:
         host = {k: torch.from_numpy(v) for k, v in plan.arrays.items()}
+    grouped = "seq_nsh" in views and shared_splits > 0
     return AttnMeta(qo_indptr=views["qo_indptr"], positions=views["positions"], seg_indptr=views["seg_indptr"],
                     seg_page_indptr=views["seg_page_indptr"], seg_offset=views["seg_offset"],
                     seg_len=views["seg_len"], seg_pos0=views["seg_pos0"], seg_delta=views["seg_delta"],
                     page_ids=views["page_ids"], num_seqs=plan.num_seqs, max_q_len=plan.max_q_len,
-                    max_kv_len=plan.max_kv_len, decode=plan.decode, num_splits=num_splits, host=host)
+                    max_kv_len=plan.max_kv_len, decode=plan.decode, num_splits=num_splits, host=host,
+                    grp_qo_indptr=views["grp_qo_indptr"] if grouped else None,
+                    grp_seg_indptr=views["grp_seg_indptr"] if grouped else None,
+                    seq_nsh=views["seq_nsh"] if grouped else None,
+                    shared_splits=shared_splits if grouped else 0,
+                    grp_max_q=plan.num_seqs if grouped else 0)

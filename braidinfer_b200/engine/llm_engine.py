@@ -104,6 +104,7 @@ class LLMEngine:
             # graphs may hold NCCL calls (TP): release them before the process group goes away
             self.model_runner.graphs.clear()
             self.model_runner.graphs_gather.clear()
+            self.model_runner.graphs_shared.clear()
             self.model_runner.prefill_graphs.clear()
             if self.model_runner.device.type == "cuda":
                 import torch

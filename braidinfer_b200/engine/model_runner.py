@@ -27,7 +27,7 @@ from ..config import Config
 from ..models import build_model
 from ..parallel.state import TPState
 from ..utils.logging import get_logger
-from .batch import FwdItem, Plan, build_plan, make_meta, pack, unpack
+from .batch import FwdItem, Plan, build_plan, find_shared_group, make_meta, pack, unpack
 from .page_manager import PageManager
 from .sequence import Sequence
 
@@ -87,6 +87,8 @@ class ModelRunner:
         # logits-all-gather variant (graphs_gather)
         self.graphs: Dict[int, _GraphSlot] = {}
         self.graphs_gather: Dict[int, _GraphSlot] = {}
+        # decode graphs for steps with a shared-prefix group, keyed (bucket, TP sampling)
+        self.graphs_shared: Dict[Tuple[int, bool], _GraphSlot] = {}
         self.sms = _num_sms(self.device)
         self.timing = {"steps": 0, "prefill_tokens": 0, "decode_tokens": 0}
         self.capture_logits: Optional[list] = None  # debug/test hook (eager steps only)
@@ -166,12 +168,14 @@ class ModelRunner:
             return t.pin_memory().to(self.device, non_blocking=True)
         return t
 
-    def forward_items(self, items: List[FwdItem]) -> torch.Tensor:
-        """Eager forward; returns final-normed hidden rows of items with ``logits=True``."""
-        plan = build_plan(items, self.page_size)
+    def forward_items(self, items: List[FwdItem], group: Optional[tuple] = None) -> torch.Tensor:
+        """Eager forward; returns final-normed hidden rows of items with ``logits=True``.
+        ``group``: shared-prefix group of a decode batch (members first)."""
+        plan = build_plan(items, self.page_size, group=group)
         views = self._upload(plan)
         ns = self._decode_splits(plan.num_seqs, plan.max_kv_len) if plan.decode else 1
-        meta = make_meta(views, plan, ns)
+        sh = self._shared_splits(plan.num_seqs, ns) if group is not None and group[0] > 0 else 0
+        meta = make_meta(views, plan, ns, shared_splits=sh)
         kv = self.page_manager.kv_cache
         h = self.model.forward(views["input_ids"], views["positions"], views["slots"], meta, kv)
         rows = h.index_select(0, views["logits_idx"].long()) if plan.sizes["logits_idx"] else h[:0]
@@ -195,9 +199,47 @@ class ModelRunner:
         return ops.sample(logits, ft[0], kt, ft[1], ft[2], lt[0], lt[1],
                           all_greedy=all(s.temperature == 0 for s in seqs))
 
+    # ------------------------------------------------- shared-prefix decode
+    def _shared_splits(self, n_seqs: int, own_splits: int) -> int:
+        """Key splits of the shared-prefix pass: about two resident CTAs per SM
+        over (64-row query tiles x KV heads), within the 32 partial slots."""
+        L = self.model.layout
+        G = max(1, L.q_heads // max(1, L.kv_heads))
+        qt = -(-n_seqs * G // 64)
+        want = max(1, (2 * self.sms) // max(1, qt * L.kv_heads))
+        return max(1, min(want, 32 - own_splits, 24))
+
+    def _shared_group(self, seqs: List[Sequence]):
+        """Reorder a decode batch so a shared-prefix group comes first; returns
+        ``(seqs, items, group)`` (``group`` None when no segment is shared)."""
+        items = self._items_for(seqs)
+        if not self.config.shared_prefix_batching or len(seqs) < 2 or not hasattr(self.model, "layout"):
+            return seqs, items, None
+        found = find_shared_group(items, self.page_size)
+        if found is None:
+            return seqs, items, None
+        members, keys = found
+        rest = [i for i in range(len(seqs)) if i not in set(members)]
+        order = members + rest
+        return [seqs[i] for i in order], [items[i] for i in order], (len(members), keys)
+
     def run(self, seqs: List[Sequence], is_prefill: bool) -> List[int]:
         """One engine step for ``seqs``; returns one sampled token per sequence."""
         self.timing["steps"] += 1
+        if not is_prefill and all(s.num_tokens > s.num_cached_tokens for s in seqs):
+            ordered, items, group = self._shared_group(seqs)
+            if group is not None:
+                out = None
+                if self.config.use_cuda_graphs and len(seqs) <= self.config.max_graph_batch:
+                    out = self._run_graph(ordered, items, group)
+                if out is None:
+                    hn = self.forward_items(items, group)
+                    out = self.sample(hn, ordered).tolist()
+                    if self.fused_comm is not None:
+                        self.fused_comm.check()
+                self.timing["decode_tokens"] += len(seqs)
+                by_id = {sq.seq_id: t for sq, t in zip(ordered, out)}
+                return [by_id[sq.seq_id] for sq in seqs]
         if not is_prefill and self.config.use_cuda_graphs and len(seqs) <= self.config.max_graph_batch:
             out = self._run_graph(seqs)
             if out is not None:
@@ -268,12 +310,16 @@ class ModelRunner:
             return False
         return all(fc.can_sample(s.temperature, s.top_k, s.top_p, s.min_p) for s in seqs)
 
-    def _capture(self, B: int, prefill_tokens: int = 0, tp_sampling: bool = False) -> _GraphSlot:
+    def _capture(self, B: int, prefill_tokens: int = 0, tp_sampling: bool = False, shared: bool = False) -> _GraphSlot:
         """Capture one engine step: a decode step of ``B`` sequences, or (with
         ``prefill_tokens``) a prefill of one sequence padded to that many tokens.
-        ``tp_sampling``: sample through the vocab-parallel record exchange."""
+        ``tp_sampling``: sample through the vocab-parallel record exchange;
+        ``shared``: decode with a shared-prefix group (the group's metadata is
+        refreshed with every replay)."""
         g = _GraphSlot()
         g.seg_cap, g.page_cap = self._graph_caps(B)
+        if shared:
+            g.seg_cap += 16  # the group's shared segments, listed once
         pm = self.page_manager
         if prefill_tokens:
             g.seg_cap, g.page_cap = g.seg_cap + 1, g.page_cap + 1  # + the padding sequence
@@ -282,12 +328,13 @@ class ModelRunner:
                               page_cap=g.page_cap, pad_tokens=prefill_tokens - 1)
         else:
             plan = build_plan([], self.page_size, pad_seqs=B, scratch_page=pm.scratch_page,
-                              seg_cap=g.seg_cap, page_cap=g.page_cap)
+                              seg_cap=g.seg_cap, page_cap=g.page_cap, group=(0, set()) if shared else None)
         g.sizes = plan.sizes
         g.meta_buf = torch.from_numpy(pack(plan)).to(self.device)
         views = unpack(g.meta_buf, g.sizes)
         g.num_splits = 1 if prefill_tokens else self._decode_splits(B)
-        meta = make_meta(views, plan, g.num_splits)
+        meta = make_meta(views, plan, g.num_splits,
+                         shared_splits=self._shared_splits(B, g.num_splits) if shared else 0)
         meta.decode = not prefill_tokens
         meta.max_q_len = prefill_tokens or 1
         meta.max_kv_len = self.config.max_model_len
@@ -340,21 +387,29 @@ class ModelRunner:
             if b <= mb and b not in self.graphs:
                 self.graphs[b] = self._capture(b, tp_sampling=tps)
 
-    def _run_graph(self, seqs: List[Sequence]) -> Optional[List[int]]:
+    def _run_graph(self, seqs: List[Sequence], items: Optional[List[FwdItem]] = None,
+                   group: Optional[tuple] = None) -> Optional[List[int]]:
         B = self._bucket(len(seqs))
         if B < 0:
             return None
         tps = self._tp_sampling(seqs)
-        if not tps and self.fused_comm is not None and self.tp.size > 1 and hasattr(self.model, "sample_tp"):
-            table = self.graphs_gather  # settings that need the whole distribution
+        if group is not None:
+            key = (B, tps)
+            g = self.graphs_shared.get(key)
+            if g is None:
+                g = self.graphs_shared[key] = self._capture(B, tp_sampling=tps, shared=True)
         else:
-            table = self.graphs
-        g = table.get(B)
-        if g is None:
-            g = table[B] = self._capture(B, tp_sampling=tps)
+            if not tps and self.fused_comm is not None and self.tp.size > 1 and hasattr(self.model, "sample_tp"):
+                table = self.graphs_gather  # settings that need the whole distribution
+            else:
+                table = self.graphs
+            g = table.get(B)
+            if g is None:
+                g = table[B] = self._capture(B, tp_sampling=tps)
         try:
-            plan = build_plan(self._items_for(seqs), self.page_size, pad_seqs=B - len(seqs),
-                              scratch_page=self.page_manager.scratch_page, seg_cap=g.seg_cap, page_cap=g.page_cap)
+            plan = build_plan(items if items is not None else self._items_for(seqs), self.page_size,
+                              pad_seqs=B - len(seqs), scratch_page=self.page_manager.scratch_page,
+                              seg_cap=g.seg_cap, page_cap=g.page_cap, group=group)
         except OverflowError:
             return None
         if plan.sizes != g.sizes:

@@ -54,6 +54,15 @@ class AttnMeta:
     num_splits: int = 1           # split-KV factor of the decode kernel
     # host copies (CPU reference path and planning)
     host: Optional[dict] = None
+    # shared-prefix decode: the group's tokens [grp_qo_indptr[0], grp_qo_indptr[1])
+    # attend once to segments [grp_seg_indptr[0], grp_seg_indptr[1]) (split into
+    # shared_splits key ranges); seq_nsh flags the member sequences, whose own
+    # segment lists leave those segments out
+    grp_qo_indptr: Optional[torch.Tensor] = None
+    grp_seg_indptr: Optional[torch.Tensor] = None
+    seq_nsh: Optional[torch.Tensor] = None
+    shared_splits: int = 0
+    grp_max_q: int = 0
 
 
 def qkv_prepare(qkv: torch.Tensor, positions: torch.Tensor, slot_mapping: torch.Tensor,
@@ -129,7 +138,11 @@ def attention_ref(q: torch.Tensor, kv_layer: torch.Tensor, meta: AttnMeta, cos: 
             continue
         pos = h["positions"][t0:t1].long()
         scores, values = [], []
-        for s in range(int(segp[b]), int(segp[b + 1])):
+        segs = list(range(int(segp[b]), int(segp[b + 1])))
+        if meta.seq_nsh is not None and int(h["seq_nsh"][b]):
+            # a shared-prefix group member: its shared segments are listed once for the group
+            segs = list(range(int(h["grp_seg_indptr"][0]), int(h["grp_seg_indptr"][1]))) + segs
+        for s in segs:
             n = int(h["seg_len"][s])
             if n == 0:
                 continue
@@ -170,6 +183,7 @@ def attention(q: torch.Tensor, kv_layer: torch.Tensor, meta: AttnMeta, cos: torc
                         meta.seg_page_indptr, meta.seg_offset, meta.seg_len, meta.seg_pos0, meta.seg_delta,
                         meta.page_ids, cos, sin, float(scale), bool(use_rope), int(meta.num_seqs),
                         int(meta.max_q_len), int(meta.max_kv_len), bool(meta.decode), int(meta.num_splits),
-                        ws.get("partial_o"), ws.get("partial_lse"))
+                        ws.get("partial_o"), ws.get("partial_lse"), meta.grp_qo_indptr, meta.grp_seg_indptr,
+                        meta.seq_nsh, int(meta.shared_splits), int(meta.grp_max_q))
         return out
     return attention_ref(q, kv_layer, meta, cos, sin, scale, use_rope)

@@ -178,6 +178,25 @@ def decode_step(model: str, B: int, plen: int) -> None:
     torch.cuda.cudart().cudaProfilerStop()
 
 
+def bench_sample(B: int, V: int, greedy: bool = True) -> dict:
+    """Device sampler over [B, V] bf16 logits (greedy, or temperature 0.8 with
+    top-k 50 / top-p 0.9); logits copies rotate so each launch reads HBM."""
+    from .. import ops
+
+    nc = _copies(B * V * 2)
+    xs = [torch.randn(B, V, device="cuda").bfloat16() for _ in range(nc)]
+    t = torch.full((B,), 0.0 if greedy else 0.8, device="cuda")
+    k = torch.full((B,), 0 if greedy else 50, device="cuda", dtype=torch.int32)
+    p = torch.full((B,), 1.0 if greedy else 0.9, device="cuda")
+    m = torch.zeros(B, device="cuda")
+    seed = torch.arange(B, device="cuda", dtype=torch.int64)
+    step = torch.zeros(B, device="cuda", dtype=torch.int64)
+    out = torch.empty(B, dtype=torch.int32, device="cuda")
+    us = _graph_time(lambda i: ops.sample(xs[i % nc], t, k, p, m, seed, step, out=out))
+    return {"kernel": "sample_kernel", "B": B, "V": V, "greedy": greedy, "us": round(us, 2),
+            "logits_TBps": round(B * V * 2 / us / 1e6, 3)}
+
+
 def gemm_trace(M: int, N: int, K: int, kind: str = "plain", rms: bool = True, splits: int = -1,
                bn: int = 0) -> dict:
     """Per-CTA phases of one decode-shaped GEMM launch that follows another
@@ -269,7 +288,7 @@ def gemm_trace(M: int, N: int, K: int, kind: str = "plain", rms: bool = True, sp
             "weight_MB": round(N * K * 2 / 1e6, 1)}
 
 
-def decode_trace(model: str, B: int, plen: int, replays: int = 5, out_path: str = "") -> dict:
+def decode_trace(model: str, B: int, plen: int, replays: int = 5, out_path: str = "", ctx: int = 0) -> dict:
     """Per-launch timeline of one graph-replayed decode step (one GPU, or every
     rank under torchrun with ``tensor_parallel_size`` = world size).
 
@@ -282,6 +301,8 @@ def decode_trace(model: str, B: int, plen: int, replays: int = 5, out_path: str 
     the predecessor, or, for a collective, the wait for the slowest peer) and
     ``release`` gaps (previous launch's end to this launch's release).  Under
     TP each rank reports; rank 0 prints all and the step time of each.
+    ``ctx > 0``: every request composes a 32-token system chunk and one shared
+    ``ctx``-token context chunk (cached once) before its ``plen``-token query.
     """
     import datetime
     import json
@@ -307,14 +328,31 @@ def decode_trace(model: str, B: int, plen: int, replays: int = 5, out_path: str 
     if n > 1:
         dist.barrier()
     page = 256
-    max_len = plen + 64 + replays + 16
-    llm = LLM(d, load_weights=False, tensor_parallel_size=n, max_num_seqs=B, max_model_len=max_len,
-              num_kvcache_blocks=B * math.ceil(max_len / page) + 8, kvcache_block_size=page,
-              max_graph_batch=B, max_num_batched_tokens=max(16384, max_len))
+    per_seq = plen + 64 + replays + 16
+    max_len = per_seq + (32 + ctx if ctx else 0)
+    pages = B * math.ceil(per_seq / page) + 8 + (math.ceil((32 + ctx) / page) if ctx else 0)
+    kw = dict(load_weights=False, tensor_parallel_size=n, max_num_seqs=B, max_model_len=max_len,
+              num_kvcache_blocks=pages, kvcache_block_size=page, max_graph_batch=B,
+              max_num_batched_tokens=max(16384, max_len, B * plen + 64))
     g = torch.Generator().manual_seed(3)
     sp = SamplingParams(temperature=0, max_tokens=replays + 16, ignore_eos=True)
-    for _ in range(B):
-        llm.add_request(torch.randint(3, llm.config.spec.vocab_size, (plen,), generator=g).tolist(), sp)
+    if ctx:
+        from .. import ChunkedLLM, ChunkType
+
+        cl = ChunkedLLM(d, **kw)
+        llm = cl.llm
+        V = llm.config.spec.vocab_size
+        rnd = lambda k: torch.randint(3, V, (k,), generator=g).tolist()  # noqa: E731
+        sysc = cl.registry.get(cl.register_chunk("system", ChunkType.SYSTEM_PROMPT, token_ids=rnd(32)))
+        shared = cl.registry.get(cl.register_chunk("shared", ChunkType.CONTEXT, token_ids=rnd(ctx)))
+        for i in range(B):
+            q = cl.registry.get(cl.register_chunk(f"q{i}", ChunkType.QUERY, token_ids=rnd(plen)))
+            cl._ensure_kv(cl._place(sysc, [shared], q))
+            llm.add_composition({"system_chunk": sysc, "context_chunks": [shared], "query_chunk": q}, sp)
+    else:
+        llm = LLM(d, **kw)
+        for _ in range(B):
+            llm.add_request(torch.randint(3, llm.config.spec.vocab_size, (plen,), generator=g).tolist(), sp)
     while llm.scheduler.waiting:
         llm.step()
     for _ in range(3):
@@ -370,7 +408,7 @@ def decode_trace(model: str, B: int, plen: int, replays: int = 5, out_path: str 
         r["count"] //= R
         for k in ("busy_us", "lead_us", "release_us"):
             r[k] = round(r[k] / R, 1)
-    res = {"rank": rank, "tp": n, "model": model, "batch": B, "prompt_len": plen, "launches": L,
+    res = {"rank": rank, "tp": n, "model": model, "batch": B, "prompt_len": plen, "shared_ctx": ctx, "launches": L,
            "step_us": round(sorted(step_us)[len(step_us) // 2], 1), "per_name": per}
     if n > 1:
         allr = [None] * n
@@ -513,6 +551,9 @@ def main(argv=None) -> None:
     tg.add_argument("--inter", type=int, default=14336)
     s = sub.add_parser("decode-step")
     s.add_argument("model"), s.add_argument("B", type=int), s.add_argument("plen", type=int)
+    sm = sub.add_parser("sample", help="device sampler over [B, V] logits")
+    sm.add_argument("B", type=int), sm.add_argument("V", type=int)
+    sm.add_argument("--sampled", action="store_true", help="temperature 0.8, top-k 50, top-p 0.9 (default greedy)")
     gt = sub.add_parser("gemm-trace", help="per-CTA phases of a decode GEMM after a predecessor GEMM")
     gt.add_argument("M", type=int), gt.add_argument("N", type=int), gt.add_argument("K", type=int)
     gt.add_argument("--kind", default="plain", choices=["plain", "swiglu", "qkv"])
@@ -522,6 +563,7 @@ def main(argv=None) -> None:
     t = sub.add_parser("decode-trace", help="per-launch timeline of a graph-replayed decode step (torchrun for TP)")
     t.add_argument("model"), t.add_argument("B", type=int), t.add_argument("plen", type=int)
     t.add_argument("--replays", type=int, default=5)
+    t.add_argument("--ctx", type=int, default=0, help="shared context chunk tokens (cascade composition)")
     t.add_argument("--out", default="", help="also write the JSON here")
     args = ap.parse_args(argv)
     if args.cmd == "gemm":
@@ -533,10 +575,12 @@ def main(argv=None) -> None:
                                         args.bn)))
     elif args.cmd == "tp-gemm":
         bench_tp_gemm(args.tokens_decode, args.tokens_prefill, args.hidden, args.inter)
+    elif args.cmd == "sample":
+        print(json.dumps(bench_sample(args.B, args.V, not args.sampled)))
     elif args.cmd == "gemm-trace":
         print(json.dumps(gemm_trace(args.M, args.N, args.K, args.kind, not args.no_rms, args.splits, args.bn)))
     elif args.cmd == "decode-trace":
-        decode_trace(args.model, args.B, args.plen, args.replays, args.out)
+        decode_trace(args.model, args.B, args.plen, args.replays, args.out, args.ctx)
     elif args.cmd == "attn-decode":
         print(json.dumps(bench_attn_decode(args.B, args.L, args.Hq, args.Hkv, args.splits)))
     elif args.cmd == "attn-prefill":

@@ -65,6 +65,15 @@ struct AttnParams {
   unsigned long long* span;   // optional launch span (profiling)
   PrefetchArgs pf;            // decode: the next GEMM's weight to pull into L2 (tensor map tmP)
   int kv_evict_first;         // decode: read K/V with the evict-first L2 policy
+  // Shared-prefix decode (segments common to a group of sequences are read
+  // once for all of them): partials live at split index split_base + split
+  // of split_stride slots per (token, head).  The shared pass (prefill kernel,
+  // partial_only) fills slots [0, split_base of the decode pass); the decode
+  // pass merges its own splits with those slots for the group's sequences.
+  int split_stride;           // partial slots per (token, head); 0: num_splits
+  int split_base;             // first slot of this launch's splits
+  int partial_only;           // prefill kernel: publish partials, do not merge
+  const int* seq_nsh;         // decode: 1 for sequences of the shared-prefix group (nullptr: none)
 };
 
 constexpr float LOG2E = 1.4426950408889634f;
@@ -493,6 +502,12 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(const __grid_consta
   }
 
   // ---- merge the 4 warps' partial states (reuse the K/V buffers)
+  // Partials: split_stride slots per (token, head); this launch's splits
+  // start at split_base; nsh shared-prefix partials of this sequence (slots
+  // [0, nsh)) were published by the shared pass before this kernel.
+  const int stride = p.split_stride > 0 ? p.split_stride : p.num_splits;
+  const int nsh = (p.seq_nsh != nullptr && p.seq_nsh[b] != 0) ? p.split_base : 0;
+  const bool direct = p.num_splits == 1 && nsh == 0;
   __syncthreads();
   if (threadIdx.x == 0)  // every K/V tile has landed: pull this CTA's share of the next GEMM's weight into L2
     prefetch_next_weight(&tmP, p.pf, (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x,
@@ -544,18 +559,18 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(const __grid_consta
     O.z *= inv;
     O.w *= inv;
     const int h = kh * G + row;
-    if (p.num_splits == 1) {
+    if (direct) {
       __nv_bfloat16* o = p.out + (size_t)t * p.Hq * D + h * D + d;
       *reinterpret_cast<__nv_bfloat162*>(o) = __floats2bfloat162_rn(O.x, O.y);
       *reinterpret_cast<__nv_bfloat162*>(o + 2) = __floats2bfloat162_rn(O.z, O.w);
     } else {
-      const size_t idx = ((size_t)t * p.Hq + h) * p.num_splits + split;
+      const size_t idx = ((size_t)t * p.Hq + h) * stride + p.split_base + split;
       *reinterpret_cast<float4*>(p.part_o + idx * D + d) = O;
       if (d == 0) p.part_lse[idx] = L > 0.f ? M + log2f(L) : -INFINITY;
     }
   }
   if (tr != nullptr && threadIdx.x == 0) tr[4] = globaltimer_ns();
-  if (p.num_splits == 1) {
+  if (direct) {
     if (threadIdx.x == 0) span_end(p.span);
     return;
   }
@@ -574,13 +589,16 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(const __grid_consta
     if (threadIdx.x == 0) span_end(p.span);
     return;
   }
-  const int ns = p.num_splits;
+  // slots [0, nsh) (shared prefix) and [split_base, split_base + num_splits) (this pass)
+  const int ns = p.split_base + p.num_splits;
+  const int sb = p.split_base;
   for (int i = threadIdx.x; i < G * (D / 4); i += 128) {
     const int row = i / (D / 4), d = (i % (D / 4)) * 4;
-    const size_t base = ((size_t)t * p.Hq + kh * G + row) * ns;
+    const size_t base = ((size_t)t * p.Hq + kh * G + row) * stride;
     float lse[32];
 #pragma unroll
-    for (int q = 0; q < 32; ++q) lse[q] = q < ns ? __ldcg(p.part_lse + base + q) : -INFINITY;
+    for (int q = 0; q < 32; ++q)
+      lse[q] = (q < ns && (q < nsh || q >= sb)) ? __ldcg(p.part_lse + base + q) : -INFINITY;
     float M = -INFINITY;
 #pragma unroll
     for (int q = 0; q < 32; ++q) M = fmaxf(M, lse[q]);
@@ -592,11 +610,13 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(const __grid_consta
         float4 o[16];
 #pragma unroll
         for (int k = 0; k < 16; ++k)
-          o[k] = q0 + k < ns ? __ldcg(reinterpret_cast<const float4*>(p.part_o + (base + q0 + k) * D + d))
-                             : make_float4(0.f, 0.f, 0.f, 0.f);
+          o[k] = (q0 + k < ns && (q0 + k < nsh || q0 + k >= sb))
+                     ? __ldcg(reinterpret_cast<const float4*>(p.part_o + (base + q0 + k) * D + d))
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
-          const float w = (M == -INFINITY || q0 + k >= ns) ? 0.f : exp2f(lse[q0 + k] - M);
+          const float w = (M == -INFINITY || q0 + k >= ns || lse[q0 + k] == -INFINITY) ? 0.f
+                                                                                         : exp2f(lse[q0 + k] - M);
           W += w;
           O.x += w * o[k].x;
           O.y += w * o[k].y;
@@ -659,8 +679,16 @@ __global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const __grid_const
   const int row0 = blockIdx.x * 64;
   if (row0 >= rows) return;
   const int nrows = min(64, rows - row0);
-  const int max_pos = p.positions[t0 + (row0 + nrows - 1) / G];
-  const int min_pos = p.positions[t0 + row0 / G];
+  int max_pos = p.positions[t0 + (row0 + nrows - 1) / G];
+  int min_pos = p.positions[t0 + row0 / G];
+  if (p.partial_only) {
+    // the rows of a shared-prefix group are decode tokens of different
+    // sequences: positions are not ordered by row
+    for (int tk = t0 + row0 / G; tk <= t0 + (row0 + nrows - 1) / G; ++tk) {
+      max_pos = max(max_pos, p.positions[tk]);
+      min_pos = min(min_pos, p.positions[tk]);
+    }
+  }
   const int gq = lane >> 2;
   int rpos[2];
 #pragma unroll
@@ -887,6 +915,27 @@ __global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const __grid_const
   }
   const int c = lane & 3;
   if (tr != nullptr && threadIdx.x == 0) tr[2] = globaltimer_ns();
+  if (p.partial_only) {
+    // shared-prefix pass: publish (normalised partial, log-sum-exp) at slot
+    // split_base + split; the decode pass merges them
+    const int stride = p.split_stride > 0 ? p.split_stride : S;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int rr = row0 + warp * 16 + gq + 8 * h;
+      if (rr >= rows) continue;
+      const int tok = t0 + rr / G, head = kh * G + rr % G;
+      const size_t idx = ((size_t)tok * p.Hq + head) * stride + p.split_base + split;
+      const float inv = l[h] > 0.f ? 1.f / l[h] : 0.f;
+      float* po = p.part_o + idx * D;
+#pragma unroll
+      for (int nb = 0; nb < D / 8; ++nb)
+        *reinterpret_cast<float2*>(po + nb * 8 + 2 * c) =
+            make_float2(acc[nb][2 * h] * inv, acc[nb][2 * h + 1] * inv);
+      if (c == 0) p.part_lse[idx] = l[h] > 0.f ? m[h] + log2f(l[h]) : -INFINITY;
+    }
+    if (threadIdx.x == 0) span_end(p.span);
+    return;
+  }
   if (S == 1) {
     // ---- normalise and store
 #pragma unroll
@@ -1098,7 +1147,9 @@ void attention(torch::Tensor out, torch::Tensor q, torch::Tensor kv, torch::Tens
                torch::Tensor seg_offset, torch::Tensor seg_len, torch::Tensor seg_pos0, torch::Tensor seg_delta,
                torch::Tensor page_ids, torch::Tensor cos, torch::Tensor sin, double scale, bool use_rope,
                int64_t num_seqs, int64_t max_q_len, int64_t max_kv_len, bool decode, int64_t num_splits,
-               c10::optional<torch::Tensor> part_o, c10::optional<torch::Tensor> part_lse) {
+               c10::optional<torch::Tensor> part_o, c10::optional<torch::Tensor> part_lse,
+               c10::optional<torch::Tensor> grp_qo_indptr, c10::optional<torch::Tensor> grp_seg_indptr,
+               c10::optional<torch::Tensor> seq_nsh, int64_t shared_splits, int64_t grp_max_q) {
   TORCH_CHECK(q.is_cuda() && q.scalar_type() == at::kBFloat16 && kv.scalar_type() == at::kBFloat16);
   TORCH_CHECK(q.is_contiguous() && kv.is_contiguous() && out.is_contiguous());
   const int T = q.size(0), Hq = q.size(1), D = q.size(2);
@@ -1153,31 +1204,61 @@ void attention(torch::Tensor out, torch::Tensor q, torch::Tensor kv, torch::Tens
     n_counters = (size_t)qt * num_seqs * Hkv;
   }
   p.trace = g_attn_trace;
-  p.span = next_span(decode ? "attn_decode" : "attn_prefill");
-  static const int kv_ef = [] {  // tuning knob: BRAID_KV_EVICT_FIRST=1 streams decode K/V evict-first
+  // Decode K/V are read once per step (shared chunk pages by CTAs running at
+  // the same time): evict-first keeps them from pushing out other lines.
+  // Tuning knob: BRAID_KV_EVICT_FIRST=0 uses the default L2 policy.
+  static const int kv_ef = [] {
     const char* e = getenv("BRAID_KV_EVICT_FIRST");
-    return e && e[0] == '1' ? 1 : 0;
+    return e && e[0] == '0' ? 0 : 1;
   }();
   p.kv_evict_first = kv_ef;
+  // Shared-prefix decode: a group of sequences whose common segments are
+  // attended once (prefill kernel over the group's decode tokens, partials
+  // only), then each sequence's own segments (decode kernel) merged with them.
+  const bool grouped = decode && shared_splits > 0 && grp_qo_indptr.has_value() && grp_qo_indptr->defined();
+  const int S_sh = grouped ? (int)shared_splits : 0;
+  const int S_tot = S_sh + p.num_splits;
+  TORCH_CHECK(S_tot <= 32, "attention: at most 32 partial slots per (token, head)");
   torch::Tensor po, pl;
-  if (p.num_splits > 1) {
-    if (part_o.has_value() && part_o->defined() && part_o->numel() >= (int64_t)T * Hq * p.num_splits * D) {
+  if (S_tot > 1) {
+    if (part_o.has_value() && part_o->defined() && part_o->numel() >= (int64_t)T * Hq * S_tot * D &&
+        part_lse.has_value() && part_lse->defined() && part_lse->numel() >= (int64_t)T * Hq * S_tot) {
       po = *part_o;
       pl = *part_lse;
     } else {
-      po = torch::empty({(int64_t)T * Hq * p.num_splits * D}, q.options().dtype(at::kFloat));
-      pl = torch::empty({(int64_t)T * Hq * p.num_splits}, q.options().dtype(at::kFloat));
+      po = torch::empty({(int64_t)T * Hq * S_tot * D}, q.options().dtype(at::kFloat));
+      pl = torch::empty({(int64_t)T * Hq * S_tot}, q.options().dtype(at::kFloat));
     }
     p.part_o = po.data_ptr<float>();
     p.part_lse = pl.data_ptr<float>();
     p.counters = attn_counters(q.get_device(), n_counters);
   }
-  if (D == 128)
-    launch_attn<128>(p, num_seqs, max_q_len, decode, T, kv.size(0), st);
-  else if (D == 64)
-    launch_attn<64>(p, num_seqs, max_q_len, decode, T, kv.size(0), st);
-  else
-    TORCH_CHECK(false, "attention: head_dim must be 64 or 128");
+  auto run = [&](AttnParams& a, int64_t nseq, int64_t mq, bool dec) {
+    if (D == 128)
+      launch_attn<128>(a, (int)nseq, (int)mq, dec, T, kv.size(0), st);
+    else if (D == 64)
+      launch_attn<64>(a, (int)nseq, (int)mq, dec, T, kv.size(0), st);
+    else
+      TORCH_CHECK(false, "attention: head_dim must be 64 or 128");
+  };
+  if (grouped) {
+    TORCH_CHECK(grp_seg_indptr.has_value() && seq_nsh.has_value() && seq_nsh->numel() >= num_seqs,
+                "attention: shared-prefix group metadata incomplete");
+    AttnParams a = p;
+    a.qo_indptr = grp_qo_indptr->data_ptr<int>();
+    a.seg_indptr = grp_seg_indptr->data_ptr<int>();
+    a.num_splits = S_sh;
+    a.split_base = 0;
+    a.split_stride = S_tot;
+    a.partial_only = 1;
+    a.span = next_span("attn_shared_prefix");
+    run(a, grp_qo_indptr->numel() - 1, std::max<int64_t>(1, grp_max_q), false);
+    p.split_base = S_sh;
+    p.split_stride = S_tot;
+    p.seq_nsh = seq_nsh->data_ptr<int>();
+  }
+  p.span = next_span(decode ? "attn_decode" : "attn_prefill");
+  run(p, num_seqs, max_q_len, decode);
 }
 
 }  // namespace braid

@@ -43,7 +43,9 @@ void attention(torch::Tensor out, torch::Tensor q, torch::Tensor kv, torch::Tens
                torch::Tensor seg_offset, torch::Tensor seg_len, torch::Tensor seg_pos0, torch::Tensor seg_delta,
                torch::Tensor page_ids, torch::Tensor cos, torch::Tensor sin, double scale, bool use_rope,
                int64_t num_seqs, int64_t max_q_len, int64_t max_kv_len, bool decode, int64_t num_splits,
-               c10::optional<torch::Tensor> part_o, c10::optional<torch::Tensor> part_lse);
+               c10::optional<torch::Tensor> part_o, c10::optional<torch::Tensor> part_lse,
+               c10::optional<torch::Tensor> grp_qo_indptr, c10::optional<torch::Tensor> grp_seg_indptr,
+               c10::optional<torch::Tensor> seq_nsh, int64_t shared_splits, int64_t grp_max_q);
 void attn_set_trace(torch::Tensor buf);
 void rms_norm(torch::Tensor out, torch::Tensor x, torch::Tensor w, double eps);
 void add_rms_norm(torch::Tensor out, torch::Tensor residual, torch::Tensor x, torch::Tensor w, double eps);
@@ -98,7 +100,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_force_bn", &braid::gemm_force_bn, "tuning: force the decode token-tile width (0 = heuristic)");
   m.def("gemm_force_splits", &braid::gemm_force_splits, "tuning: force the split-K factor (0 = heuristic)");
   m.def("gemm_check_error", &braid::gemm_check_error, "read and clear the GEMM bounded-wait error flag");
-  m.def("attention", &braid::attention, "paged cascade attention (decode/prefill)");
+  m.def("attention", &braid::attention, "paged cascade attention (decode/prefill; decode with a shared-prefix group)",
+        py::arg("out"), py::arg("q"), py::arg("kv"), py::arg("qo_indptr"), py::arg("positions"),
+        py::arg("seg_indptr"), py::arg("seg_page_indptr"), py::arg("seg_offset"), py::arg("seg_len"),
+        py::arg("seg_pos0"), py::arg("seg_delta"), py::arg("page_ids"), py::arg("cos"), py::arg("sin"),
+        py::arg("scale"), py::arg("use_rope"), py::arg("num_seqs"), py::arg("max_q_len"), py::arg("max_kv_len"),
+        py::arg("decode"), py::arg("num_splits"), py::arg("part_o") = py::none(), py::arg("part_lse") = py::none(),
+        py::arg("grp_qo_indptr") = py::none(), py::arg("grp_seg_indptr") = py::none(),
+        py::arg("seq_nsh") = py::none(), py::arg("shared_splits") = 0, py::arg("grp_max_q") = 0);
   m.def("attn_set_trace", &braid::attn_set_trace, "profiling: per-CTA phase timestamps of later decode attention");
   m.def("rms_norm", &braid::rms_norm);
   m.def("add_rms_norm", &braid::add_rms_norm);
