@@ -360,7 +360,11 @@ def decode_trace(model: str, B: int, plen: int, replays: int = 5, out_path: str 
     runner = llm.model_runner
     C = ext()
     buf = torch.zeros(4 * 4096, dtype=torch.int64, device="cuda")
+    # force a re-capture of this bucket (whichever graph table the step uses)
     runner.graphs.pop(B, None)
+    runner.graphs_gather.pop(B, None)
+    for k in [k for k in runner.graphs_shared if k[0] == B]:
+        runner.graphs_shared.pop(k)
     C.span_trace(buf)
     llm.step()  # re-captures the bucket with span slots baked into the launches
     names = C.span_names()

@@ -310,3 +310,48 @@ def test_sampler_greedy_and_filters():
     assert out[2].item() in top5
     # same hash on both sides: identical draws
     assert out.cpu().tolist() == ref.tolist()
+
+
+@pytest.mark.parametrize("D,G", [(128, 4), (128, 8), (64, 8)])
+@pytest.mark.parametrize("own_splits,shared_splits", [(1, 5), (2, 9)])
+def test_attention_shared_prefix_decode(D, G, own_splits, shared_splits):
+    """Decode where five of seven sequences compose the same cached chunks at
+    the same positions: the shared segments are attended once for the group
+    (prefill kernel over the group's tokens, partials only) and merged with
+    each sequence's private keys by the decode kernel.  Checked against the
+    fp32 restatement of the ungrouped plan."""
+    from braidinfer_b200 import ops
+    from braidinfer_b200.engine.batch import FwdItem, build_plan, find_shared_group, make_meta, pack, unpack
+    from braidinfer_b200.engine.sequence import SegmentRef
+    PS, P, Hkv = 16, 512, 2
+    Hq = Hkv * G
+    sys_seg = SegmentRef(pages=[0], offset=0, length=10, pos0=0, delta=0)
+    ctx = SegmentRef(pages=list(range(1, 21)), offset=0, length=300, pos0=10, delta=3)
+    ctx_moved = SegmentRef(pages=list(range(1, 21)), offset=0, length=300, pos0=20, delta=13)
+    items, nxt = [], 40
+    for b, plen in enumerate([5, 17, 1, 33, 9, 12, 40]):
+        member = b not in (2, 5)
+        segs = [sys_seg, ctx] if member else [ctx_moved]
+        base = 310 if member else 320
+        pages = list(range(nxt, nxt + 3))
+        nxt += 3
+        items.append(FwdItem(tokens=[1], pos0=base + plen - 1, priv_index0=plen - 1, priv_pages=pages,
+                             priv_pos0=base, segments=segs))
+    members, keys = find_shared_group(items, PS)
+    assert sorted(members) == [0, 1, 3, 4, 6]
+    order = members + [i for i in range(len(items)) if i not in members]
+    items = [items[i] for i in order]
+    plan_g = build_plan(items, PS, group=(len(members), keys))
+    plan_u = build_plan(items, PS)
+    views = unpack(torch.from_numpy(pack(plan_g)).to(DEV), plan_g.sizes)
+    meta_g = make_meta(views, plan_g, own_splits, shared_splits=shared_splits)
+    meta_u = make_meta(unpack(torch.from_numpy(pack(plan_u)), plan_u.sizes), plan_u)
+    g = torch.Generator(device=DEV).manual_seed(D + G)
+    kv = torch.randn(P, 2, Hkv, PS, D, device=DEV, generator=g).bfloat16()
+    q = torch.randn(len(items), Hq, D, device=DEV, generator=g).bfloat16()
+    cos, sin = ops.build_cos_sin(D, 10000.0, 2048, device=DEV)
+    for _ in range(2):  # the partial slots are reused call after call
+        out = ops.attention(q, kv, meta_g, cos, sin, D ** -0.5, True)
+        torch.cuda.synchronize()
+    ref = ops.attention_ref(q.cpu().float(), kv.cpu().float(), meta_u, cos.cpu(), sin.cpu(), D ** -0.5, True)
+    torch.testing.assert_close(out.float().cpu(), ref.float(), atol=2e-2, rtol=2e-2)
