@@ -90,6 +90,40 @@ BRAID_DEVICE float ld<__nv_bfloat16>(const __nv_bfloat16* p, size_t i) { return 
 template <>
 BRAID_DEVICE float ld<float>(const float* p, size_t i) { return p[i]; }
 
+// Block-wide argmax of x[0, n) (ids id0 + i): 16-byte loads when the row is
+// 16-byte aligned, scalar loads for the tail.
+BRAID_DEVICE ArgMax row_argmax(const __nv_bfloat16* x, int n, int id0) {
+  ArgMax a{-INFINITY, 0x7fffffff};
+  int head = 0;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    head = n & ~7;
+    for (int i = threadIdx.x * 8; i < head; i += SNT * 8) {
+      const uint4 u = *reinterpret_cast<const uint4*>(x + i);
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) a = better(a, ArgMax{bf2f(e[j]), id0 + i + j});
+    }
+  }
+  for (int i = head + threadIdx.x; i < n; i += SNT) a = better(a, ArgMax{bf2f(x[i]), id0 + i});
+  return a;
+}
+BRAID_DEVICE ArgMax row_argmax(const float* x, int n, int id0) {
+  ArgMax a{-INFINITY, 0x7fffffff};
+  int head = 0;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    head = n & ~3;
+    for (int i = threadIdx.x * 4; i < head; i += SNT * 4) {
+      const float4 u = *reinterpret_cast<const float4*>(x + i);
+      a = better(a, ArgMax{u.x, id0 + i});
+      a = better(a, ArgMax{u.y, id0 + i + 1});
+      a = better(a, ArgMax{u.z, id0 + i + 2});
+      a = better(a, ArgMax{u.w, id0 + i + 3});
+    }
+  }
+  for (int i = head + threadIdx.x; i < n; i += SNT) a = better(a, ArgMax{x[i], id0 + i});
+  return a;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(SNT) sample_kernel(int* __restrict__ out, const T* __restrict__ logits, int V,
                                                      int ld_row, const float* __restrict__ temperature,
@@ -104,8 +138,7 @@ __global__ void __launch_bounds__(SNT) sample_kernel(int* __restrict__ out, cons
   const T* x = logits + (size_t)row * ld_row;
   const float temp = all_greedy ? 0.f : temperature[row];
   if (temp <= 0.f) {
-    ArgMax a{-INFINITY, 0x7fffffff};
-    for (int i = threadIdx.x; i < V; i += SNT) a = better(a, ArgMax{ld(x, i), i});
+    ArgMax a = row_argmax(x, V, 0);
     a = block_argmax(a, ared);
     if (threadIdx.x == 0) {
       out[row] = a.i;
@@ -257,13 +290,15 @@ __global__ void __launch_bounds__(SNT) tp_sample_kernel(
     s_n = 0;
     s_fail = 0;
   }
-  // ---- local record
+  // ---- local record (the z max only matters for the top-k candidates)
   float zmax = -INFINITY;
-  for (int i = threadIdx.x; i < nvalid; i += SNT) zmax = fmaxf(zmax, bf2f(x[i]) * inv_t);
-  zmax = block_reduce_max(zmax, fred);
+  if (!greedy && k > 0) {
+    for (int i = threadIdx.x; i < nvalid; i += SNT) zmax = fmaxf(zmax, bf2f(x[i]) * inv_t);
+    zmax = block_reduce_max(zmax, fred);
+  }
   ArgMax a{-INFINITY, 0x7fffffff};
   if (greedy) {
-    for (int i = threadIdx.x; i < nvalid; i += SNT) a = better(a, ArgMax{bf2f(x[i]), vocab_start + i});
+    a = row_argmax(x, nvalid, vocab_start);
   } else if (k <= 0) {
     const uint64_t key = mix64((uint64_t)seed[row] ^ mix64((uint64_t)step[row]));
     for (int i = threadIdx.x; i < nvalid; i += SNT) {
@@ -284,15 +319,21 @@ __global__ void __launch_bounds__(SNT) tp_sample_kernel(
       c = block_reduce_sum(c, fred);
       if (c >= (float)want) lo = mid; else hi = mid;
     }
-    for (int i = threadIdx.x; i < nvalid; i += SNT) {
-      const float z = bf2f(x[i]) * inv_t;
-      if (z >= lo) {
-        const int j = atomicAdd(&s_n, 1);
-        if (j < TPS_KC) {
-          rec.cz[j] = z;
-          rec.cid[j] = vocab_start + i;
+    // Values >= hi are fewer than `want`: take all of them first, then fill
+    // the remaining slots with values in [lo, hi) (ties at the boundary), so
+    // an overflow of ties can never push out a larger value.
+    for (int pass = 0; pass < 2; ++pass) {
+      for (int i = threadIdx.x; i < nvalid; i += SNT) {
+        const float z = bf2f(x[i]) * inv_t;
+        if (pass == 0 ? z >= hi : (z >= lo && z < hi)) {
+          const int j = atomicAdd(&s_n, 1);
+          if (j < TPS_KC) {
+            rec.cz[j] = z;
+            rec.cid[j] = vocab_start + i;
+          }
         }
       }
+      __syncthreads();
     }
   }
   __syncthreads();
