@@ -32,52 +32,13 @@
 #include "common.cuh"
 #include "launch.cuh"
 #include "tmap.h"
+#include "attention_types.cuh"
 
 #include <mutex>
 #include <unordered_map>
 
 namespace braid {
 
-struct AttnParams {
-  const __nv_bfloat16* q;  // [T, Hq, D] unrotated
-  const __nv_bfloat16* kv; // layer pool [P, 2, Hkv, PS, D]
-  __nv_bfloat16* out;      // [T, Hq*D]
-  const int* qo_indptr;
-  const int* positions;
-  const int* seg_indptr;
-  const int* seg_page_indptr;
-  const int* seg_offset;
-  const int* seg_len;
-  const int* seg_pos0;
-  const int* seg_delta;
-  const int* page_ids;
-  const float* cos;
-  const float* sin;
-  float scale_log2;
-  int use_rope;
-  int rope_len;
-  int Hq, Hkv, G, PS;
-  int num_splits;
-  float* part_o;    // [T, Hq, splits, D]
-  float* part_lse;  // [T, Hq, splits]
-  int* counters;    // [T * Hkv] split arrival counters, kept at zero between launches
-  unsigned long long* trace;  // optional per-CTA phase timestamps (profiling)
-  unsigned long long* span;   // optional launch span (profiling)
-  PrefetchArgs pf;            // decode: the next GEMM's weight to pull into L2 (tensor map tmP)
-  int kv_evict_first;         // decode: read K/V with the evict-first L2 policy
-  // Shared-prefix decode (segments common to a group of sequences are read
-  // once for all of them): partials live at split index split_base + split
-  // of split_stride slots per (token, head).  The shared pass (prefill kernel,
-  // partial_only) fills slots [0, split_base of the decode pass); the decode
-  // pass merges its own splits with those slots for the group's sequences.
-  int split_stride;           // partial slots per (token, head); 0: num_splits
-  int split_base;             // first slot of this launch's splits
-  int partial_only;           // prefill kernel: publish partials, do not merge
-  const int* seq_nsh;         // decode: 1 for sequences of the shared-prefix group (nullptr: none)
-};
-
-constexpr float LOG2E = 1.4426950408889634f;
-constexpr int KT = 64;  // keys per tile
 
 // byte offset of 16-byte chunk c of row r in a swizzled [rows x D] bf16 tile
 template <int D>
@@ -1084,9 +1045,17 @@ static int* attn_counters(int dev, size_t n) {
   return e.first;
 }
 
+bool attn_prefill_tc_enabled(int D);
+int attn_prefill_tc_rows();
+void launch_attn_prefill_tc(const AttnParams& p, int num_seqs, int max_q_len, int64_t P, cudaStream_t st);
+
 template <int D>
 static void launch_attn(AttnParams& p, int num_seqs, int max_q_len, bool decode, int T, int64_t P,
                         cudaStream_t st) {
+  if (!decode && attn_prefill_tc_enabled(D)) {  // tcgen05 prefill (attention_tc.cu)
+    launch_attn_prefill_tc(p, num_seqs, max_q_len, P, st);
+    return;
+  }
   if (decode) {
     constexpr int STAGES = D == 128 ? 3 : 4;
     const int smem = 2 * STAGES * KT * D * 2 + 16 * D * 2 + 2 * STAGES * 8 + 1024;
@@ -1189,7 +1158,8 @@ void attention(torch::Tensor out, torch::Tensor q, torch::Tensor kv, torch::Tens
   } else {
     // Prefill: split the keys when the q tiles alone leave SMs idle (a short
     // query over long cached chunks); each split keeps >= 2 key tiles.
-    const int qt = (int)((max_q_len * G + 63) / 64);
+    const int tile_rows = attn_prefill_tc_enabled(D) ? attn_prefill_tc_rows() : 64;
+    const int qt = (int)((max_q_len * G + tile_rows - 1) / tile_rows);
     const int64_t work = (int64_t)qt * num_seqs * Hkv;
     static const int forced = [] {  // tuning knob: BRAID_PREFILL_SPLITS=n
       const char* e = getenv("BRAID_PREFILL_SPLITS");

@@ -12,7 +12,7 @@ from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 SRC = [os.path.join("csrc", f) for f in (
-    "bindings.cpp", "gemm_tcgen05.cu", "gemm_persistent.cu", "attention.cu", "elementwise.cu", "sampling.cu", "comm.cu")]
+    "bindings.cpp", "gemm_tcgen05.cu", "gemm_persistent.cu", "attention.cu", "attention_tc.cu", "elementwise.cu", "sampling.cu", "comm.cu")]
 
 NVCC = ["-O3", "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-std=c++17",
         "--expt-relaxed-constexpr", "-U__CUDA_NO_HALF_OPERATORS__", "-U__CUDA_NO_BFLOAT16_CONVERSIONS__",

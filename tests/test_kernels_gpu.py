@@ -355,3 +355,42 @@ def test_attention_shared_prefix_decode(D, G, own_splits, shared_splits):
         torch.cuda.synchronize()
     ref = ops.attention_ref(q.cpu().float(), kv.cpu().float(), meta_u, cos.cpu(), sin.cpu(), D ** -0.5, True)
     torch.testing.assert_close(out.float().cpu(), ref.float(), atol=2e-2, rtol=2e-2)
+
+
+@pytest.mark.parametrize("splits", [1, 4])
+@pytest.mark.parametrize("G", [1, 4, 8])
+@pytest.mark.parametrize("tc", ["1", "0"])
+def test_attention_prefill_pages256(G, splits, tc):
+    """Prefill with head_dim 128 on the tcgen05 kernel (attention_tc.cu, the
+    default) and on the mma.sync kernel (a child process with
+    BRAID_ATTN_TC=0); 256-token pages take the 64-row TMA box path.  Segments
+    with RoPE deltas, offsets into their first page, a long causal private
+    segment (several 128-key tiles, several 128-row query tiles) and a
+    1-token sequence."""
+    import os
+    import subprocess
+    import sys
+    if tc == "0":
+        env = dict(os.environ, BRAID_ATTN_TC="0")
+        code = f"import tests.test_kernels_gpu as t; t._prefill_pages256({G}, {splits})"
+        p = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600,
+                           cwd=os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+        assert p.returncode == 0, p.stderr[-3000:]
+        return
+    _prefill_pages256(G, splits)
+
+
+def _prefill_pages256(G, splits):
+    from braidinfer_b200 import ops
+    PS, P, Hkv = 256, 64, 2
+    Hq = Hkv * G
+    seqs = [(300, [(130, 0, 7), (260, 40, -5), (300, 0, 0)]), (1, [(1, 0, 0)]), (77, [(500, 0, 0), (77, 0, 0)])]
+    meta, T = _rand_plan(seqs, PS, P, DEV, False)
+    meta.num_splits = splits
+    g = torch.Generator(device=DEV).manual_seed(G * 10 + splits)
+    kv = torch.randn(P, 2, Hkv, PS, 128, device=DEV, generator=g).bfloat16()
+    q = torch.randn(T, Hq, 128, device=DEV, generator=g).bfloat16()
+    cos, sin = ops.build_cos_sin(128, 500000.0, 4096, device=DEV)
+    out = ops.attention(q, kv, meta, cos, sin, 128 ** -0.5, True)
+    ref = ops.attention_ref(q.cpu().float(), kv.cpu().float(), meta, cos.cpu(), sin.cpu(), 128 ** -0.5, True)
+    torch.testing.assert_close(out.float().cpu(), ref.float(), atol=2e-2, rtol=2e-2)
