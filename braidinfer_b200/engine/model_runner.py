@@ -201,12 +201,19 @@ class ModelRunner:
 
     # ------------------------------------------------- shared-prefix decode
     def _shared_splits(self, n_seqs: int, own_splits: int) -> int:
-        """Key splits of the shared-prefix pass: about two resident CTAs per SM
-        over (64-row query tiles x KV heads), within the 32 partial slots."""
+        """Key splits of the shared-prefix pass: about one wave of resident
+        CTAs over (query tiles x KV heads), within the 32 partial slots.  The
+        tcgen05 prefill kernel takes 256-row tiles at one CTA per SM, the
+        mma.sync kernel 64-row tiles at two."""
         L = self.model.layout
         G = max(1, L.q_heads // max(1, L.kv_heads))
-        qt = -(-n_seqs * G // 64)
-        want = max(1, (2 * self.sms) // max(1, qt * L.kv_heads))
+        rows = 64
+        if self.device.type == "cuda":
+            from ..ops._ext import ext
+            rows = int(ext().attn_prefill_tile_rows(L.head_dim))
+        per_sm = 1 if rows > 64 else 2
+        qt = -(-n_seqs * G // rows)
+        want = max(1, (per_sm * self.sms) // max(1, qt * L.kv_heads))
         return max(1, min(want, 32 - own_splits, 24))
 
     def _shared_group(self, seqs: List[Sequence]):

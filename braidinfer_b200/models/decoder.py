@@ -36,6 +36,8 @@ from ..parallel.layout import TPLayout
 from ..parallel.state import TPState
 
 PREFETCH_ALL = os.environ.get("BRAID_PREFETCH_ALL", "0") == "1"
+# decode attention pulls the o_proj weight into L2 while it streams K/V
+PREFETCH_ATTN = os.environ.get("BRAID_PREFETCH_ATTN", "0") == "1"
 
 
 class LayerWeights:
@@ -260,6 +262,8 @@ class DecoderLM:
             q = ops.qkv_gemm(residual, w.qkv_w, w.qkv_b, eps, positions, slot_mapping, kv_cache[i], L.q_heads,
                              L.kv_heads, S.head_dim, self.cos, self.sin, w.q_norm, w.k_norm, eps, S.use_rope)
             gu_done = nxt(w.gu_w, T)
+            if PREFETCH_ATTN and not PREFETCH_ALL:
+                ops.prefetch_next(w.o_w, T)
             o = ops.attention(q, kv_cache[i], meta, self.cos, self.sin, self.scale, S.use_rope, workspace)
             residual = self._row_parallel(o, w.o_w, residual, w.gu_w, gu_done)
             nxt(w.down_w, T)

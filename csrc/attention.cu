@@ -329,6 +329,11 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(const __grid_consta
       pc_next(p, pc, r0, r1);
       v = pc.s < pc.s1;
     }
+    // K/V streaming leaves HBM bandwidth unused: the next GEMM's weight can
+    // come into L2 alongside it
+    if (p.pf_early && lane == 0)
+      prefetch_next_weight(&tmP, p.pf, (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x,
+                           gridDim.x * gridDim.y * gridDim.z);
   }
 
   float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
@@ -470,7 +475,7 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(const __grid_consta
   const int nsh = (p.seq_nsh != nullptr && p.seq_nsh[b] != 0) ? p.split_base : 0;
   const bool direct = p.num_splits == 1 && nsh == 0;
   __syncthreads();
-  if (threadIdx.x == 0)  // every K/V tile has landed: pull this CTA's share of the next GEMM's weight into L2
+  if (threadIdx.x == 0 && !p.pf_early)  // every K/V tile has landed: pull this CTA's share of the next GEMM's weight into L2
     prefetch_next_weight(&tmP, p.pf, (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x,
                          gridDim.x * gridDim.y * gridDim.z);
   if (tr != nullptr && threadIdx.x == 0) tr[3] = globaltimer_ns();
@@ -1182,6 +1187,11 @@ void attention(torch::Tensor out, torch::Tensor q, torch::Tensor kv, torch::Tens
     return e && e[0] == '0' ? 0 : 1;
   }();
   p.kv_evict_first = kv_ef;
+  static const int pf_early = [] {  // tuning knob: BRAID_ATTN_PF_EARLY=1
+    const char* e = getenv("BRAID_ATTN_PF_EARLY");
+    return e && e[0] == '1' ? 1 : 0;
+  }();
+  p.pf_early = pf_early;
   // Shared-prefix decode: a group of sequences whose common segments are
   // attended once (prefill kernel over the group's decode tokens, partials
   // only), then each sequence's own segments (decode kernel) merged with them.

@@ -3,22 +3,27 @@
 // a request's prompt over cached chunks, and the shared-prefix pass of a
 // batched decode step.
 //
-// One CTA owns 128 query rows, each a (token, head-of-the-KV-group) pair of
-// one sequence (or of one shared-prefix group), against one KV head:
+// One CTA owns 256 query rows, each a (token, head-of-the-KV-group) pair of
+// one sequence (or of one shared-prefix group), as two 128-row Q tiles
+// against one KV head.  Tensor memory (512 columns):
+//   [0, 128)    S(0) = Q(0) K^T, fp32; P(0) as bf16 pairs in its columns [64, 128)
+//   [128, 256)  S(1), P(1)
+//   [256, 384)  O(0) += P(0) V   (P read from tensor memory, V MN-major from smem)
+//   [384, 512)  O(1)
+// Warp roles (10 warps):
 //   warp 0      TMA producer: 128-key K and V tiles of the paged KV cache
-//               (128-byte swizzle) into a 2-stage mbarrier ring
-//   warp 1      MMA issuer (one elected lane):
-//                 S = Q K^T   M=128, N=128 keys, K=128 dims -> TMEM cols [0,128)
-//                 O_t = P V   M=128, N=128 dims, K=128 keys -> TMEM cols [128,256)
-//               (V is read as an MN-major operand: the cache stores keys as rows)
-//   warps 2..5  one query row per thread (TMEM lane): build the rotated query
-//               tile (differential RoPE per segment), online softmax in base 2
-//               on S read with tcgen05.ld, P written to shared memory as bf16
-//               (K-major, 128-byte swizzle), O accumulated in registers from
-//               each O_t, then the output or the split partial.
-// Per tile j: S(j) -> softmax(j) (waits O_t(j-1), rescales O, writes P(j)) ->
-// P V(j) issued together with S(j+1).
-//
+//               (128-byte swizzle), separate 2-stage K and V rings
+//   warp 1      MMA issuer (one lane), per key tile j in the order
+//                 P(0,j)V, S(0,j+1), P(1,j)V, S(1,j+1)
+//               so the tensor core runs one tile's MMAs while the other
+//               tile's softmax warps work
+//   warps 2..5  softmax of Q tile 0, warps 6..9 of Q tile 1: one row per
+//               thread (its TMEM lane); the rotated query row (differential
+//               RoPE per segment) is built into shared memory; per key tile
+//               one read of the S row, masks only on boundary tiles, ex2,
+//               P stored back as bf16; the running maximum moves only when a
+//               tile's exceeds it by more than 2^8, and only then is O
+//               rescaled in tensor memory
 // Same semantics and output modes as attn_prefill_kernel (attention.cu):
 // key j of segment s is visible to a row at position p iff seg_pos0[s]+j <= p;
 // with num_splits > 1 each CTA covers one range of the visible keys and the
@@ -35,17 +40,20 @@
 
 namespace braid {
 
-constexpr int TC_D = 128;       // head dim
-constexpr int TC_ROWS = 128;    // query rows per CTA (MMA M)
-constexpr int TC_KEYS = 128;    // keys per tile (MMA N of S, K of P V)
-constexpr int TC_STAGES = 2;    // K/V ring depth
+constexpr int TC_D = 128;          // head dim
+constexpr int TC_ROWS = 128;       // query rows per Q tile (MMA M)
+constexpr int TC_QT = 2;           // Q tiles per CTA
+constexpr int TC_CTA_ROWS = TC_QT * TC_ROWS;
+constexpr int TC_KEYS = 128;       // keys per tile (MMA N of S, K of P V)
+constexpr int TC_STAGES = 2;       // depth of the K ring and of the V ring
+constexpr int TC_P_COL = 64;       // P(t) columns within S(t)
+constexpr int TC_THREADS = 64 + 128 * TC_QT;
 constexpr int TC_HALF = TC_KEYS * 128;  // bytes of one 64-column half of a 128-row bf16 tile (16 KB)
 constexpr int TC_TILE = 2 * TC_HALF;    // one 128 x 128 bf16 tile (32 KB)
 
 struct TcSmem {
-  static constexpr int Q = 0;                              // [2 halves][128 rows][128 B]
-  static constexpr int P = Q + TC_TILE;                    // [2 key halves][128 rows][128 B]
-  static constexpr int K = P + TC_TILE;                    // [stage][2 dim halves][128 keys][128 B]
+  static constexpr int Q = 0;                              // [Q tile][2 halves][128 rows][128 B]
+  static constexpr int K = Q + TC_QT * TC_TILE;            // [stage][2 dim halves][128 keys][128 B]
   static constexpr int V = K + TC_STAGES * TC_TILE;        // same layout
   static constexpr int BAR = V + TC_STAGES * TC_TILE;
   static constexpr int TOTAL = BAR + 256 + 1024;           // barriers + TMEM address, 1024 alignment slack
@@ -155,34 +163,73 @@ BRAID_DEVICE void tc_build_q_row(const AttnParams& p, uint8_t* qs, int r, bool l
   }
 }
 
-template <int BR>
-__global__ void __launch_bounds__(192, 1) attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmkv,
-                                                                 const AttnParams p) {
+// Barrier block of the kernel (8-byte mbarriers, then the TMEM address).
+struct TcBars {
+  uint64_t kfull[TC_STAGES], kempty[TC_STAGES];  // K tile landed / both S MMAs of it completed
+  uint64_t vfull[TC_STAGES], vempty[TC_STAGES];  // V tile landed / both P V MMAs of it completed
+  uint64_t sfull[TC_QT];                         // S(t, j) in TMEM (and every earlier MMA of the CTA done)
+  uint64_t pready[TC_QT];                        // 128 arrivals: completion 0 = Q(t) built, j + 1 = P(t, j) in TMEM
+  uint64_t odone[TC_QT];                         // the last P V of tile t completed
+  uint32_t tmem;
+};
+
+// ex2.approx with flush-to-zero: the MUFU exponential, -inf -> 0.
+BRAID_DEVICE float tc_ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+static_assert(sizeof(TcBars) <= 256, "barrier block exceeds its shared-memory slot");
+static_assert(TcSmem::TOTAL <= 227 * 1024, "shared memory per CTA");
+
+// 2^x on the FMA and integer pipes, for the share of the softmax exponentials
+// taken off the MUFU unit (16 per clock per SM, which at head_dim 128 is as
+// slow as the tensor core): x = n + f with n = round(x) (the 1.5 * 2^23
+// addition leaves n in the low mantissa bits) and f in [-0.5, 0.5];
+// 2^f ~ c0 + c1 f + c2 f^2 + c3 f^3, coefficients fitted for this kernel by
+// iteratively reweighted least squares on Chebyshev nodes (maximum relative
+// error 7.5e-5, a 26th of a bf16 half-ulp); 2^n added to the exponent field.
+// x < -126 (masked keys, -inf) gives exactly 0.
+BRAID_DEVICE float tc_exp2_poly(float x) {
+  const float xc = fmaxf(x, -126.f);
+  const float t = xc + 12582912.f;
+  const float f = xc - (t - 12582912.f);
+  const float q = fmaf(fmaf(fmaf(0.0551716573f, f, 0.2426111400f), f, 0.6932609677f), f, 0.9999280572f);
+  const float y = __int_as_float(__float_as_int(q) + ((__float_as_int(t) - 0x4B400000) << 23));
+  return x < -126.f ? 0.f : y;
+}
+
+// POLY: every POLY-th exponential of a row runs tc_exp2_poly (0: none).
+template <int BR, int POLY>
+__global__ void __launch_bounds__(TC_THREADS, 1) attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmkv,
+                                                                        const AttnParams p) {
   extern __shared__ uint8_t sm_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* qs = sm + TcSmem::Q;
-  uint8_t* ps = sm + TcSmem::P;
   uint8_t* kst = sm + TcSmem::K;
   uint8_t* vst = sm + TcSmem::V;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + TcSmem::BAR);
-  uint64_t* kfull = bars;                 // [TC_STAGES]: K and V of a tile landed
-  uint64_t* kempty = bars + TC_STAGES;    // [TC_STAGES]: the P V of that tile completed
-  uint64_t* s_full = bars + 2 * TC_STAGES;
-  uint64_t* o_full = s_full + 1;
-  uint64_t* pq = s_full + 2;              // 128 arrivals: completion 0 = Q tile, j + 1 = P(j)
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(s_full + 3);
+  TcBars& bar = *reinterpret_cast<TcBars*>(sm + TcSmem::BAR);
   __shared__ int s_abort, s_last;
 
   const int S = p.num_splits;
-  const int b = blockIdx.y, kh = blockIdx.z / S, split = blockIdx.z % S;
+  // Blocks are dispatched in linear order: the q tile is the slowest index
+  // and runs backwards, so the CTAs with the most causal keys (late query
+  // tiles of every head and sequence) start in the first wave and the short
+  // ones fill the tail.
+  const int yz = gridDim.y * gridDim.z;
+  const int lin = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  const int qtile = gridDim.x - 1 - lin / yz;
+  const int b = (lin % yz) % gridDim.y, z = (lin % yz) / gridDim.y;
+  const int kh = z / S, split = z % S;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.G;
   const int t0 = p.qo_indptr[b], nt = p.qo_indptr[b + 1] - t0;
   const int rows = nt * G;
-  const int row0 = blockIdx.x * TC_ROWS;
+  const int row0 = qtile * TC_CTA_ROWS;
   if (row0 >= rows) return;
-  const int nrows = min(TC_ROWS, rows - row0);
-  // positions of the tile's rows (not ordered by row for shared-prefix groups)
+  const int nrows = min(TC_CTA_ROWS, rows - row0);
+  const int nq = nrows > TC_ROWS ? 2 : 1;  // Q tiles with live rows (CTA-uniform)
+  // largest position among the CTA's rows (rows of a shared-prefix group are not ordered)
   TcRange rg;
   {
     int mx = -(1 << 30);
@@ -206,214 +253,333 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_tc_kernel(const __grid_co
     span_start(p.span);
     tma_prefetch_desc(&tmkv);
     for (int i = 0; i < TC_STAGES; ++i) {
-      mbar_init(&kfull[i], 1);
-      mbar_init(&kempty[i], 1);
+      mbar_init(&bar.kfull[i], 1);
+      mbar_init(&bar.kempty[i], 1);
+      mbar_init(&bar.vfull[i], 1);
+      mbar_init(&bar.vempty[i], 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(o_full, 1);
-    mbar_init(pq, 128);
+    for (int t = 0; t < TC_QT; ++t) {
+      mbar_init(&bar.sfull[t], 1);
+      mbar_init(&bar.pready[t], 128);
+      mbar_init(&bar.odone[t], 1);
+    }
     fence_barrier_init();
     s_abort = 0;
   }
   if (warp == 1) {
-    tmem_alloc(tmem_holder, 256);
+    tmem_alloc(&bar.tmem, 512);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_holder;
+  const uint32_t tmem = bar.tmem;
   pdl_trigger();
 
   TcWalk w{s0, s1, 0, 0, 0, 0, 0};
   bool more = tc_settle(p, rg, w);
-  // softmax warps: one query row per thread, the row's TMEM lane
-  const int q4 = warp & 3;
-  const int r = q4 * 32 + lane;
-  const int rr = row0 + r;
-  const bool live = warp >= 2 && r < nrows;
-  const int tok = t0 + (live ? rr / G : 0), head = kh * G + (live ? rr % G : 0);
-  const int rpos = live ? p.positions[tok] : -1;
-  const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
-  float O[TC_D];
-#pragma unroll
-  for (int d = 0; d < TC_D; ++d) O[d] = 0.f;
-  float m_run = -INFINITY, l_run = 0.f;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0 && more) {
       pdl_wait();
-      int j = 0;
+      int j = 0, kiss = 0, viss = 0;
       while (more) {
         const int st = j % TC_STAGES;
-        if (j >= TC_STAGES && !mbar_wait(&kempty[st], ((j / TC_STAGES) & 1) ^ 1)) {
-          s_abort = 1;
-          break;
-        }
-        mbar_arrive_expect_tx(&kfull[st], 2 * TC_TILE);
+        const uint32_t ph = ((j / TC_STAGES) & 1) ^ 1;
         const int* pages = p.page_ids + p.seg_page_indptr[w.s];
         const int npages = p.seg_page_indptr[w.s + 1] - p.seg_page_indptr[w.s];
+        int rk[TC_KEYS / BR];
 #pragma unroll
         for (int q = 0; q < TC_KEYS / BR; ++q) {
           const int slot = w.sl + q * BR;
           const int page = pages[min(slot / p.PS, npages - 1)];
-          const int row_k = ((page * 2 + 0) * p.Hkv + kh) * p.PS + slot % p.PS;
-          const int row_v = row_k + p.Hkv * p.PS;
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            tma_load_2d(kst + st * TC_TILE + h * TC_HALF + q * BR * 128, &tmkv, &kfull[st], h * 64, row_k);
-            tma_load_2d(vst + st * TC_TILE + h * TC_HALF + q * BR * 128, &tmkv, &kfull[st], h * 64, row_v);
-          }
+          rk[q] = ((page * 2 + 0) * p.Hkv + kh) * p.PS + slot % p.PS;
         }
+        if (j >= TC_STAGES && !mbar_wait(&bar.kempty[st], ph)) {
+          s_abort = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&bar.kfull[st], TC_TILE);
+#pragma unroll
+        for (int q = 0; q < TC_KEYS / BR; ++q)
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+            tma_load_2d(kst + st * TC_TILE + h * TC_HALF + q * BR * 128, &tmkv, &bar.kfull[st], h * 64, rk[q]);
+        ++kiss;
+        if (j >= TC_STAGES && !mbar_wait(&bar.vempty[st], ph)) {
+          s_abort = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&bar.vfull[st], TC_TILE);
+#pragma unroll
+        for (int q = 0; q < TC_KEYS / BR; ++q)
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+            tma_load_2d(vst + st * TC_TILE + h * TC_HALF + q * BR * 128, &tmkv, &bar.vfull[st], h * 64,
+                        rk[q] + p.Hkv * p.PS);
+        ++viss;
         bool ns;
         more = tc_next(p, rg, w, &ns);
         ++j;
       }
-      // every copy this CTA issued has landed before the CTA can finish (a
-      // consumer that gave up would otherwise leave copies in flight)
-      for (int i = max(0, j - TC_STAGES); i < j; ++i)
-        if (!mbar_wait(&kfull[i % TC_STAGES], (i / TC_STAGES) & 1)) s_abort = 1;
+      // every copy this CTA issued lands before the CTA can finish (a consumer
+      // that gave up would otherwise leave copies in flight)
+      for (int i = max(0, kiss - TC_STAGES); i < kiss; ++i)
+        if (!mbar_wait(&bar.kfull[i % TC_STAGES], (i / TC_STAGES) & 1)) s_abort = 1;
+      for (int i = max(0, viss - TC_STAGES); i < viss; ++i)
+        if (!mbar_wait(&bar.vfull[i % TC_STAGES], (i / TC_STAGES) & 1)) s_abort = 1;
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && more) {
       constexpr uint32_t idS = idesc_bf16_f32(TC_ROWS, TC_KEYS);
       constexpr uint32_t idPV = idesc_bf16_f32(TC_ROWS, TC_D) | (1u << 16);  // B (V) MN-major
-      int j = 0;
-      bool ok = mbar_wait(pq, 0);  // Q tile written
-      while (more && ok) {
-        const int st = j % TC_STAGES;
-        if (!mbar_wait(&kfull[st], (j / TC_STAGES) & 1)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
+      auto issue_s = [&](int t, int st) {
+        const uint8_t* qs = sm + TcSmem::Q + t * TC_TILE;
 #pragma unroll
         for (int k = 0; k < TC_D / 16; ++k) {
           const uint64_t a = smem_desc_sw128(smem_u32(qs + (k >> 2) * TC_HALF)) + 2 * (k & 3);
           const uint64_t bd = smem_desc_sw128(smem_u32(kst + st * TC_TILE + (k >> 2) * TC_HALF)) + 2 * (k & 3);
-          tc_mma_bf16(tmem, a, bd, idS, k > 0 ? 1u : 0u);
+          tc_mma_bf16(tmem + t * TC_KEYS, a, bd, idS, k > 0 ? 1u : 0u);
         }
-        tc_commit(s_full);
-        if (!mbar_wait(pq, (j + 1) & 1)) {  // P(j) written (and Q rebuilt for the next segment)
+      };
+      auto issue_pv = [&](int t, int st, bool acc) {
+#pragma unroll
+        for (int k = 0; k < TC_KEYS / 16; ++k) {
+          const uint64_t bv = smem_desc_sw128_mn(smem_u32(vst + st * TC_TILE + k * 2048), TC_HALF, 1024);
+          tc_mma_bf16_ta(tmem + 2 * TC_KEYS + t * TC_D, tmem + t * TC_KEYS + TC_P_COL + k * 8, bv, idPV,
+                         (acc || k > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = true;
+      for (int t = 0; t < nq && ok; ++t) ok = mbar_wait(&bar.pready[t], 0);  // Q tiles built
+      ok = ok && mbar_wait(&bar.kfull[0], 0);
+      if (ok) {
+        tc_fence_after();
+        for (int t = 0; t < nq; ++t) {
+          issue_s(t, 0);
+          tc_commit(&bar.sfull[t]);
+        }
+        tc_commit(&bar.kempty[0]);
+      }
+      int j = 0;
+      while (ok) {
+        const int st = j % TC_STAGES, st1 = (j + 1) % TC_STAGES;
+        bool ns;
+        const bool nxt = tc_next(p, rg, w, &ns);
+        if (!mbar_wait(&bar.vfull[st], (j / TC_STAGES) & 1)) {
           ok = false;
           break;
         }
-        tc_fence_after();
-#pragma unroll
-        for (int k = 0; k < TC_KEYS / 16; ++k) {
-          const uint64_t a = smem_desc_sw128(smem_u32(ps + (k >> 2) * TC_HALF)) + 2 * (k & 3);
-          const uint64_t bv = smem_desc_sw128_mn(smem_u32(vst + st * TC_TILE + k * 2048), TC_HALF, 1024);
-          tc_mma_bf16(tmem + TC_KEYS, a, bv, idPV, k > 0 ? 1u : 0u);
+        // tile t: P(t, j) V(j), then S(t, j + 1) into the same columns (the
+        // MMAs of one thread execute in issue order)
+        for (int t = 0; t < nq && ok; ++t) {
+          if (!mbar_wait(&bar.pready[t], (j + 1) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv(t, st, j > 0);
+          if (nxt) {
+            if (t == 0 && !mbar_wait(&bar.kfull[st1], ((j + 1) / TC_STAGES) & 1)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_s(t, st1);
+            tc_commit(&bar.sfull[t]);
+          } else {
+            tc_commit(&bar.odone[t]);
+          }
         }
-        tc_commit(o_full);
-        tc_commit(&kempty[st]);
-        bool ns;
-        more = tc_next(p, rg, w, &ns);
+        if (!ok) break;
+        tc_commit(&bar.vempty[st]);
+        if (!nxt) break;
+        tc_commit(&bar.kempty[st1]);
         ++j;
       }
       if (!ok) s_abort = 1;
     }
-  } else if (more) {
+  } else {
     // ------------------------------------------------------------ softmax
-    pdl_wait();
-    tc_build_q_row(p, qs, r, live, tok, head, rpos, p.seg_delta[w.s]);
-    fence_proxy_async_smem();
-    mbar_arrive(pq);
-    int j = 0;
-    while (more) {
-      const int pos0 = p.seg_pos0[w.s], j0 = w.sl - w.off, lo = w.lo, hi = w.hi;
-      if (!mbar_wait(s_full, j & 1)) {
-        s_abort = 1;
-        break;
+    const int t = (warp - 2) >> 2;  // Q tile of this warpgroup
+    if (t < nq) {
+      const int q4 = warp & 3;        // TMEM lane quarter this warp may access
+      const int r = q4 * 32 + lane;   // row within the Q tile = TMEM lane
+      const int rr = row0 + t * TC_ROWS + r;
+      const bool live = rr < rows;
+      const int tok = t0 + (live ? rr / G : 0), head = kh * G + (live ? rr % G : 0);
+      const int rpos = live ? p.positions[tok] : -1;
+      const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+      const uint32_t tS = tmem + lane_off + t * TC_KEYS;
+      const uint32_t tO = tmem + lane_off + 2 * TC_KEYS + t * TC_D;
+      uint8_t* qs = sm + TcSmem::Q + t * TC_TILE;
+      const float sl2 = p.scale_log2;
+      float m_run = -INFINITY, l_run = 0.f;
+      int j = 0;
+      if (more) {
+        pdl_wait();
+        tc_build_q_row(p, qs, r, live, tok, head, rpos, p.seg_delta[w.s]);
+        fence_proxy_async_smem();
+        mbar_arrive(&bar.pready[t]);
       }
-      tc_fence_after();
-      // pass 1: this tile's row maximum over visible keys (base-2 scaled logits)
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c0 = 0; c0 < TC_KEYS; c0 += 16) {
-        float v[16];
-        tmem_ld16(trow + c0, v);
-        tc_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int key = j0 + c0 + i;
-          if (live && key >= lo && key < hi && pos0 + key <= rpos) mx = fmaxf(mx, v[i] * p.scale_log2);
-        }
-      }
-      const float m_new = fmaxf(m_run, mx);
-      // O_t(j-1) = P(j-1) V(j-1) is relative to m_run: add it, then rescale to m_new
-      if (j > 0) {
-        if (!mbar_wait(o_full, (j - 1) & 1)) {
+      while (more) {
+        const int pos0 = p.seg_pos0[w.s], j0 = w.sl - w.off, lo = w.lo, hi = w.hi;
+        if (!mbar_wait(&bar.sfull[t], j & 1)) {
           s_abort = 1;
           break;
         }
         tc_fence_after();
+        uint32_t sr[TC_KEYS];
 #pragma unroll
-        for (int c0 = 0; c0 < TC_D; c0 += 16) {
-          float v[16];
-          tmem_ld16(trow + TC_KEYS + c0, v);
-          tc_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) O[c0 + i] += v[i];
-        }
-      }
-      const float alpha = (m_run == -INFINITY || m_new == -INFINITY) ? 1.f : exp2f(m_run - m_new);
-#pragma unroll
-      for (int d = 0; d < TC_D; ++d) O[d] *= alpha;
-      l_run *= alpha;
-      // pass 2: P(j) = exp2(s - m_new) as bf16 into the swizzled P tile
-#pragma unroll
-      for (int c0 = 0; c0 < TC_KEYS; c0 += 16) {
-        float v[16];
-        tmem_ld16(trow + c0, v);
+        for (int c = 0; c < TC_KEYS / 32; ++c) tmem_ld32(tS + c * 32, sr + c * 32);
         tc_wait_ld();
-        uint32_t pk[8];
+        // keys outside [lo, hi) of the segment, or after the row's position,
+        // are masked; interior tiles (every key visible to this row) skip it
+        if (live && !(j0 >= lo && j0 + TC_KEYS <= hi && pos0 + j0 + TC_KEYS - 1 <= rpos)) {
 #pragma unroll
-        for (int i = 0; i < 16; i += 2) {
-          float e[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int key = j0 + c0 + i + u;
-            const bool vis = live && key >= lo && key < hi && pos0 + key <= rpos && m_new != -INFINITY;
-            e[u] = vis ? exp2f(v[i + u] * p.scale_log2 - m_new) : 0.f;
+          for (int i = 0; i < TC_KEYS; ++i) {
+            const int key = j0 + i;
+            if (!(key >= lo && key < hi && pos0 + key <= rpos)) sr[i] = __float_as_uint(-INFINITY);
           }
-          const __nv_bfloat162 h2 = __floats2bfloat162_rn(e[0], e[1]);
-          // the sum uses the rounded values the tensor core multiplies
-          l_run += __low2float(h2) + __high2float(h2);
-          pk[i / 2] = *reinterpret_cast<const uint32_t*>(&h2);
         }
+        // eight independent partial maxima (a 128-long dependent chain otherwise)
+        float m8[8];
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
-          *reinterpret_cast<uint4*>(ps + tc_off(r, c0 / 8 + c)) =
-              make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+        for (int u = 0; u < 8; ++u) m8[u] = __uint_as_float(sr[u]);
+#pragma unroll
+        for (int i = 8; i < TC_KEYS; ++i) m8[i & 7] = fmaxf(m8[i & 7], __uint_as_float(sr[i]));
+        const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                               fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+        // running maximum (base 2) moves only when the tile's exceeds it by
+        // more than 8: P <= 2^8 stays exact enough in bf16 and fp32 sums, and
+        // O in TMEM is rescaled rarely
+        const float m_new = fmaxf(m_run, mx * sl2);
+        const bool resc = m_new > m_run + 8.f;
+        const float alpha = resc ? tc_ex2(m_run - m_new) : 1.f;
+        if (resc) {
+          l_run *= alpha;
+          m_run = m_new;
+        }
+        const float mneg = m_run == -INFINITY ? 0.f : -m_run;
+        float l8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int i = 0; i < TC_KEYS / 2; ++i) {
+          const float x0 = fmaf(__uint_as_float(sr[2 * i]), sl2, mneg);
+          const float x1 = fmaf(__uint_as_float(sr[2 * i + 1]), sl2, mneg);
+          const float e0 = (POLY > 0 && (2 * i) % POLY == POLY - 1) ? tc_exp2_poly(x0) : tc_ex2(x0);
+          const float e1 = (POLY > 0 && (2 * i + 1) % POLY == POLY - 1) ? tc_exp2_poly(x1) : tc_ex2(x1);
+          l8[i & 7] += e0 + e1;
+          sr[i] = pack_bf16(e0, e1);
+        }
+        l_run += ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7]));
+        // P(t, j) as bf16 pairs into columns [TC_P_COL, TC_P_COL + 64) of S(t)
+        tmem_st32(tS + TC_P_COL, sr);
+        tmem_st32(tS + TC_P_COL + 32, sr + 32);
+        if (__any_sync(0xffffffffu, resc && j > 0)) {
+          // O(t) holds P V of tiles < j (complete: S(t, j) was issued after
+          // them) and P(t, j) V is not issued before this thread's arrival
+#pragma unroll 1
+          for (int c = 0; c < TC_D / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + c * 32, o);
+            tc_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(tO + c * 32, o);
+          }
+        }
+        tc_wait_st();
+        bool ns;
+        more = tc_next(p, rg, w, &ns);
+        // S(t, j) is consumed and S(t, j + 1) waits for this arrival: the next
+        // segment's rotated queries can replace the Q tile now
+        if (more && ns) tc_build_q_row(p, qs, r, live, tok, head, rpos, p.seg_delta[w.s]);
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(&bar.pready[t]);
+        ++j;
       }
-      m_run = m_new;
-      bool ns;
-      more = tc_next(p, rg, w, &ns);
-      // S(j) is consumed and S(j+1) is not issued before this arrival: the
-      // next segment's rotated queries can replace the Q tile now
-      if (more && ns) tc_build_q_row(p, qs, r, live, tok, head, rpos, p.seg_delta[w.s]);
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(pq);
-      ++j;
-    }
-    // the last tile's P V
-    if (j > 0 && !s_abort) {
-      if (mbar_wait(o_full, (j - 1) & 1)) {
-        tc_fence_after();
-#pragma unroll
-        for (int c0 = 0; c0 < TC_D; c0 += 16) {
-          float v[16];
-          tmem_ld16(trow + TC_KEYS + c0, v);
+      const bool have = j > 0 && !s_abort;
+      if (have && !mbar_wait(&bar.odone[t], 0)) s_abort = 1;
+      tc_fence_after();
+      // ------------------------------------------------------------ output
+      const bool direct = S == 1 && !p.partial_only;
+      const int stride = p.split_stride > 0 ? p.split_stride : S;
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      const size_t idx = ((size_t)tok * p.Hq + head) * stride + p.split_base + split;
+#pragma unroll 1
+      for (int c = 0; c < TC_D / 32; ++c) {
+        uint32_t o[32];
+        if (have) {
+          tmem_ld32(tO + c * 32, o);
           tc_wait_ld();
+        } else {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) O[c0 + i] += v[i];
+          for (int i = 0; i < 32; ++i) o[i] = 0u;
         }
-      } else {
-        s_abort = 1;
+        if (!live || s_abort) continue;
+        if (direct) {
+          __nv_bfloat16* out = p.out + ((size_t)tok * p.Hq + head) * TC_D + c * 32;
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            *reinterpret_cast<uint4*>(out + u * 8) = make_uint4(
+                pack_bf16(__uint_as_float(o[8 * u]) * inv, __uint_as_float(o[8 * u + 1]) * inv),
+                pack_bf16(__uint_as_float(o[8 * u + 2]) * inv, __uint_as_float(o[8 * u + 3]) * inv),
+                pack_bf16(__uint_as_float(o[8 * u + 4]) * inv, __uint_as_float(o[8 * u + 5]) * inv),
+                pack_bf16(__uint_as_float(o[8 * u + 6]) * inv, __uint_as_float(o[8 * u + 7]) * inv));
+        } else {
+          float* po = p.part_o + idx * TC_D + c * 32;
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            *reinterpret_cast<float4*>(po + 4 * u) =
+                make_float4(__uint_as_float(o[4 * u]) * inv, __uint_as_float(o[4 * u + 1]) * inv,
+                            __uint_as_float(o[4 * u + 2]) * inv, __uint_as_float(o[4 * u + 3]) * inv);
+        }
+      }
+      if (live && !s_abort && !direct) p.part_lse[idx] = l_run > 0.f ? m_run + log2f(l_run) : -INFINITY;
+      if (!direct && !p.partial_only) {
+        // the last split CTA of this q tile merges every split's partial
+        named_bar_sync(1, 128 * nq);
+        if (threadIdx.x == 64) {
+          int* ctr = p.counters + ((size_t)b * p.Hkv + kh) * gridDim.x + qtile;
+          const int old = atomic_add_acq_rel_gpu(ctr, 1);  // releases this CTA's partials, acquires the others'
+          s_last = old == S - 1;
+          if (s_last) *ctr = 0;
+        }
+        named_bar_sync(1, 128 * nq);
+        if (s_last && live) {
+          const size_t base = ((size_t)tok * p.Hq + head) * stride;
+          float wq[32];
+          float mxl = -INFINITY;
+#pragma unroll
+          for (int q = 0; q < 32; ++q) {
+            wq[q] = q < S ? __ldcg(p.part_lse + base + q) : -INFINITY;
+            mxl = fmaxf(mxl, wq[q]);
+          }
+          float sum = 0.f;
+#pragma unroll
+          for (int q = 0; q < 32; ++q) {
+            wq[q] = (mxl == -INFINITY || wq[q] == -INFINITY) ? 0.f : exp2f(wq[q] - mxl);
+            sum += wq[q];
+          }
+          const float winv = sum > 0.f ? 1.f / sum : 0.f;
+          __nv_bfloat16* o = p.out + ((size_t)tok * p.Hq + head) * TC_D;
+          for (int d = 0; d < TC_D; d += 4) {
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int q = 0; q < S; ++q) {
+              if (wq[q] == 0.f) continue;
+              const float4 v = __ldcg(reinterpret_cast<const float4*>(p.part_o + (base + q) * TC_D + d));
+              acc.x += wq[q] * v.x;
+              acc.y += wq[q] * v.y;
+              acc.z += wq[q] * v.z;
+              acc.w += wq[q] * v.w;
+            }
+            *reinterpret_cast<__nv_bfloat162*>(o + d) = __floats2bfloat162_rn(acc.x * winv, acc.y * winv);
+            *reinterpret_cast<__nv_bfloat162*>(o + d + 2) = __floats2bfloat162_rn(acc.z * winv, acc.w * winv);
+          }
+        }
       }
     }
   }
@@ -421,77 +587,7 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_tc_kernel(const __grid_co
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
-  }
-  if (warp >= 2) {
-    // ------------------------------------------------------------ output
-    const bool direct = S == 1 && !p.partial_only;
-    const int stride = p.split_stride > 0 ? p.split_stride : S;
-    const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-    if (live && !s_abort) {
-      if (direct) {
-        __nv_bfloat16* o = p.out + ((size_t)tok * p.Hq + head) * TC_D;
-#pragma unroll
-        for (int c = 0; c < TC_D / 8; ++c) {
-          uint32_t pk[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const __nv_bfloat162 h2 = __floats2bfloat162_rn(O[c * 8 + 2 * u] * inv, O[c * 8 + 2 * u + 1] * inv);
-            pk[u] = *reinterpret_cast<const uint32_t*>(&h2);
-          }
-          *reinterpret_cast<uint4*>(o + c * 8) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        }
-      } else {
-        const size_t idx = ((size_t)tok * p.Hq + head) * stride + p.split_base + split;
-        float* po = p.part_o + idx * TC_D;
-#pragma unroll
-        for (int d = 0; d < TC_D; d += 4)
-          *reinterpret_cast<float4*>(po + d) = make_float4(O[d] * inv, O[d + 1] * inv, O[d + 2] * inv, O[d + 3] * inv);
-        p.part_lse[idx] = l_run > 0.f ? m_run + log2f(l_run) : -INFINITY;
-      }
-    }
-    if (!direct && !p.partial_only) {
-      // the last split CTA of this q tile merges every split's partial
-      named_bar_sync(1, 128);
-      if (threadIdx.x == 64) {
-        int* ctr = p.counters + ((size_t)b * p.Hkv + kh) * gridDim.x + blockIdx.x;
-        const int old = atomic_add_acq_rel_gpu(ctr, 1);  // releases this CTA's partials, acquires the others'
-        s_last = old == S - 1;
-        if (s_last) *ctr = 0;
-      }
-      named_bar_sync(1, 128);
-      if (s_last && live) {
-        const size_t base = ((size_t)tok * p.Hq + head) * stride;
-        float wq[32];
-        float mx = -INFINITY;
-#pragma unroll
-        for (int q = 0; q < 32; ++q) {
-          wq[q] = q < S ? __ldcg(p.part_lse + base + q) : -INFINITY;
-          mx = fmaxf(mx, wq[q]);
-        }
-        float sum = 0.f;
-#pragma unroll
-        for (int q = 0; q < 32; ++q) {
-          wq[q] = (mx == -INFINITY || wq[q] == -INFINITY) ? 0.f : exp2f(wq[q] - mx);
-          sum += wq[q];
-        }
-        const float winv = sum > 0.f ? 1.f / sum : 0.f;
-        __nv_bfloat16* o = p.out + ((size_t)tok * p.Hq + head) * TC_D;
-        for (int d = 0; d < TC_D; d += 4) {
-          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-          for (int q = 0; q < S; ++q) {
-            if (wq[q] == 0.f) continue;
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(p.part_o + (base + q) * TC_D + d));
-            acc.x += wq[q] * v.x;
-            acc.y += wq[q] * v.y;
-            acc.z += wq[q] * v.z;
-            acc.w += wq[q] * v.w;
-          }
-          *reinterpret_cast<__nv_bfloat162*>(o + d) = __floats2bfloat162_rn(acc.x * winv, acc.y * winv);
-          *reinterpret_cast<__nv_bfloat162*>(o + d + 2) = __floats2bfloat162_rn(acc.z * winv, acc.w * winv);
-        }
-      }
-    }
+    tmem_dealloc(tmem, 512);
   }
   if (threadIdx.x == 0) span_end(p.span);
 }
@@ -502,39 +598,60 @@ namespace braid {
 
 CUtensorMap make_tmap(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows);
 
-// tcgen05 prefill for head_dim 128 (BRAID_ATTN_TC=0 keeps the mma.sync
-// kernel).  Measured on B200, L = 2048 causal, 32 q / 8 KV heads: 170 us
-// against 356 us for the mma.sync kernel.
+// Prefill kernel choice for head_dim 128: -1 follows BRAID_ATTN_TC (1 selects
+// this kernel, anything else the mma.sync kernel of attention.cu); 0 / 1 set by
+// attn_select_prefill_tc.
+static int g_attn_tc = -1;
+
+void attn_select_prefill_tc(int64_t mode) { g_attn_tc = mode < 0 ? -1 : (mode ? 1 : 0); }
+
+// Share of the tcgen05 prefill softmax exponentials computed by polynomial
+// (every n-th of a row; 0 none; -1 follows BRAID_ATTN_POLY); 256-token pages.
+static int g_attn_poly = -1;
+void attn_set_exp2_poly(int64_t n) { g_attn_poly = n < 0 ? -1 : (n == 2 || n == 4 ? (int)n : 0); }
+
 bool attn_prefill_tc_enabled(int D) {
-  static const bool on = [] {
+  static const bool env_on = [] {
     const char* e = getenv("BRAID_ATTN_TC");
-    return !(e && e[0] == '0');
+    return e && e[0] == '1';
   }();
+  const bool on = g_attn_tc < 0 ? env_on : g_attn_tc == 1;
   return on && D == TC_D;
 }
 
-int attn_prefill_tc_rows() { return TC_ROWS; }
+int attn_prefill_tc_rows() { return TC_CTA_ROWS; }
+
+// Query rows per CTA of the prefill kernel that serves head_dim D (the
+// tcgen05 kernel holds one CTA per SM, the mma.sync kernel two).
+int64_t attn_prefill_tile_rows(int64_t D) { return attn_prefill_tc_enabled((int)D) ? TC_CTA_ROWS : 64; }
 
 void launch_attn_prefill_tc(const AttnParams& p, int num_seqs, int max_q_len, int64_t P, cudaStream_t st) {
   const int64_t rows = P * 2 * p.Hkv * p.PS;  // the layer pool as rows of head_dim elements
-  const int qt = (max_q_len * p.G + TC_ROWS - 1) / TC_ROWS;
+  const int qt = (max_q_len * p.G + TC_CTA_ROWS - 1) / TC_CTA_ROWS;
   const dim3 grid(qt, num_seqs, p.Hkv * p.num_splits);
+  static const int env_poly = [] {  // tuning knob: BRAID_ATTN_POLY = 0, 2 or 4
+    const char* e = getenv("BRAID_ATTN_POLY");
+    return e ? atoi(e) : 0;
+  }();
+  const int poly = g_attn_poly >= 0 ? g_attn_poly : env_poly;
+  auto go = [&](auto k, int br) {
+    static bool attr[8] = {};
+    const int slot = (br == 64 ? 4 : 0) + (poly == 2 ? 1 : poly == 4 ? 2 : 0);
+    if (!attr[slot]) {
+      C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, TcSmem::TOTAL));
+      attr[slot] = true;
+    }
+    launch_pdl(k, grid, dim3(TC_THREADS), TcSmem::TOTAL, st, make_tmap(p.kv, rows, TC_D, TC_D, br), p);
+  };
   if (p.PS % 64 == 0) {
-    auto k = attn_prefill_tc_kernel<64>;
-    static bool attr = false;
-    if (!attr) {
-      C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, TcSmem::TOTAL));
-      attr = true;
-    }
-    launch_pdl(k, grid, dim3(192), TcSmem::TOTAL, st, make_tmap(p.kv, rows, TC_D, TC_D, 64), p);
+    if (poly == 2)
+      go(attn_prefill_tc_kernel<64, 2>, 64);
+    else if (poly == 4)
+      go(attn_prefill_tc_kernel<64, 4>, 64);
+    else
+      go(attn_prefill_tc_kernel<64, 0>, 64);
   } else {
-    auto k = attn_prefill_tc_kernel<16>;
-    static bool attr = false;
-    if (!attr) {
-      C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, TcSmem::TOTAL));
-      attr = true;
-    }
-    launch_pdl(k, grid, dim3(192), TcSmem::TOTAL, st, make_tmap(p.kv, rows, TC_D, TC_D, 16), p);
+    go(attn_prefill_tc_kernel<16, 0>, 16);
   }
 }
 

@@ -35,6 +35,7 @@ struct AttnParams {
   unsigned long long* trace;  // optional per-CTA phase timestamps (profiling)
   unsigned long long* span;   // optional launch span (profiling)
   PrefetchArgs pf;            // decode: the next GEMM's weight to pull into L2 (tensor map tmP)
+  int pf_early;               // decode: issue that prefetch with the first K/V tiles (else after the last)
   int kv_evict_first;         // decode: read K/V with the evict-first L2 policy
   // Shared-prefix decode (segments common to a group of sequences are read
   // once for all of them): partials live at split index split_base + split

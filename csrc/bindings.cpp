@@ -47,6 +47,9 @@ void attention(torch::Tensor out, torch::Tensor q, torch::Tensor kv, torch::Tens
                c10::optional<torch::Tensor> grp_qo_indptr, c10::optional<torch::Tensor> grp_seg_indptr,
                c10::optional<torch::Tensor> seq_nsh, int64_t shared_splits, int64_t grp_max_q);
 void attn_set_trace(torch::Tensor buf);
+void attn_select_prefill_tc(int64_t mode);
+int64_t attn_prefill_tile_rows(int64_t D);
+void attn_set_exp2_poly(int64_t n);
 void rms_norm(torch::Tensor out, torch::Tensor x, torch::Tensor w, double eps);
 void add_rms_norm(torch::Tensor out, torch::Tensor residual, torch::Tensor x, torch::Tensor w, double eps);
 void layer_norm(torch::Tensor out, torch::Tensor x, torch::Tensor w, torch::Tensor b, double eps);
@@ -108,6 +111,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("decode"), py::arg("num_splits"), py::arg("part_o") = py::none(), py::arg("part_lse") = py::none(),
         py::arg("grp_qo_indptr") = py::none(), py::arg("grp_seg_indptr") = py::none(),
         py::arg("seq_nsh") = py::none(), py::arg("shared_splits") = 0, py::arg("grp_max_q") = 0);
+  m.def("attn_prefill_tile_rows", &braid::attn_prefill_tile_rows,
+        "query rows per CTA of the prefill attention kernel for head_dim D (256: tcgen05, one CTA per SM; 64: mma.sync, two)");
+  m.def("attn_set_exp2_poly", &braid::attn_set_exp2_poly,
+        "tcgen05 prefill softmax: every n-th exponential by polynomial on the FMA pipe (n = 0, 2, 4; -1: BRAID_ATTN_POLY)");
+  m.def("attn_select_prefill_tc", &braid::attn_select_prefill_tc,
+        "prefill attention for head_dim 128: 1 tcgen05 kernel, 0 mma.sync kernel, -1 BRAID_ATTN_TC");
   m.def("attn_set_trace", &braid::attn_set_trace, "profiling: per-CTA phase timestamps of later decode attention");
   m.def("rms_norm", &braid::rms_norm);
   m.def("add_rms_norm", &braid::add_rms_norm);

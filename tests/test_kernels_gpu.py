@@ -18,6 +18,15 @@ def _check_err():
     assert _ext().gemm_check_error(torch.cuda.current_device()) == 0
 
 
+@pytest.fixture(params=[1, 0], ids=["tc", "mma"])
+def prefill_kernel(request):
+    """Runs the test on each prefill attention kernel for head_dim 128: the
+    tcgen05 kernel (attention_tc.cu) and the mma.sync kernel (attention.cu)."""
+    _ext().attn_select_prefill_tc(request.param)
+    yield request.param
+    _ext().attn_select_prefill_tc(-1)
+
+
 @pytest.mark.parametrize("M,N,K", [(1, 256, 512), (7, 4096, 1024), (16, 1536, 2048), (33, 640, 256),
                                    (64, 2048, 4096), (65, 384, 512), (200, 1024, 1024), (1000, 2560, 2048),
                                    (513, 6144, 4096)])
@@ -257,7 +266,7 @@ def test_attention_decode(D, G, splits):
 
 @pytest.mark.parametrize("D,G", [(64, 8), (128, 2), (128, 4)])
 @pytest.mark.parametrize("splits", [1, 3, 7])
-def test_attention_prefill(D, G, splits):
+def test_attention_prefill(D, G, splits, prefill_kernel):
     """splits > 1: keys divided over CTAs, partials merged by the last CTA."""
     from braidinfer_b200 import ops
     PS, P, Hkv = 16, 1024, 2
@@ -276,7 +285,7 @@ def test_attention_prefill(D, G, splits):
 
 
 @pytest.mark.parametrize("D,G", [(64, 8), (128, 4)])
-def test_attention_prefill_short_query_long_context(D, G):
+def test_attention_prefill_short_query_long_context(D, G, prefill_kernel):
     """A short query over long cached chunks picks key splits automatically."""
     from braidinfer_b200 import ops
     PS, P, Hkv = 16, 1024, 2
@@ -314,7 +323,7 @@ def test_sampler_greedy_and_filters():
 
 @pytest.mark.parametrize("D,G", [(128, 4), (128, 8), (64, 8)])
 @pytest.mark.parametrize("own_splits,shared_splits", [(1, 5), (2, 9)])
-def test_attention_shared_prefix_decode(D, G, own_splits, shared_splits):
+def test_attention_shared_prefix_decode(D, G, own_splits, shared_splits, prefill_kernel):
     """Decode where five of seven sequences compose the same cached chunks at
     the same positions: the shared segments are attended once for the group
     (prefill kernel over the group's tokens, partials only) and merged with
@@ -359,25 +368,47 @@ def test_attention_shared_prefix_decode(D, G, own_splits, shared_splits):
 
 @pytest.mark.parametrize("splits", [1, 4])
 @pytest.mark.parametrize("G", [1, 4, 8])
-@pytest.mark.parametrize("tc", ["1", "0"])
-def test_attention_prefill_pages256(G, splits, tc):
-    """Prefill with head_dim 128 on the tcgen05 kernel (attention_tc.cu, the
-    default) and on the mma.sync kernel (a child process with
-    BRAID_ATTN_TC=0); 256-token pages take the 64-row TMA box path.  Segments
-    with RoPE deltas, offsets into their first page, a long causal private
-    segment (several 128-key tiles, several 128-row query tiles) and a
-    1-token sequence."""
-    import os
-    import subprocess
-    import sys
-    if tc == "0":
-        env = dict(os.environ, BRAID_ATTN_TC="0")
-        code = f"import tests.test_kernels_gpu as t; t._prefill_pages256({G}, {splits})"
-        p = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600,
-                           cwd=os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
-        assert p.returncode == 0, p.stderr[-3000:]
-        return
-    _prefill_pages256(G, splits)
+@pytest.mark.parametrize("poly", [0, 2, 4])
+def test_attention_prefill_pages256(G, splits, prefill_kernel, poly):
+    """Prefill with head_dim 128 and 256-token pages (64-row TMA boxes):
+    segments with RoPE deltas, offsets into their first page, a long causal
+    private segment (several 128-key tiles, several query tiles) and a
+    1-token sequence.  ``poly``: share of the tcgen05 softmax exponentials
+    computed by polynomial (every 2nd / 4th)."""
+    if poly and not prefill_kernel:
+        pytest.skip("the polynomial share applies to the tcgen05 kernel")
+    _ext().attn_set_exp2_poly(poly)
+    try:
+        _prefill_pages256(G, splits)
+    finally:
+        _ext().attn_set_exp2_poly(-1)
+
+
+@pytest.mark.parametrize("splits", [1, 2])
+def test_attention_prefill_growing_scores(splits, prefill_kernel):
+    """Scores that grow along the keys (key norms ramp up): the row maximum
+    rises by far more than 2^8 per 128-key tile, so the tcgen05 kernel
+    rescales O in tensor memory on every tile."""
+    from braidinfer_b200 import ops
+    PS, P, Hkv, G, D = 16, 128, 2, 4, 128
+    seqs = [(600, [(600, 0, 0)]), (130, [(70, 0, 3), (130, 0, 0)])]
+    meta, T = _rand_plan(seqs, PS, P, DEV, False)
+    meta.num_splits = splits
+    g = torch.Generator(device=DEV).manual_seed(5)
+    kv = torch.randn(P, 2, Hkv, PS, D, device=DEV, generator=g).abs()
+    h = meta.host
+    ramp = torch.ones(P, PS)
+    for si in range(len(h["seg_len"])):  # key norm grows with the key's position in its sequence
+        pg0, off, pos0 = int(h["seg_page_indptr"][si]), int(h["seg_offset"][si]), int(h["seg_pos0"][si])
+        for i in range(int(h["seg_len"][si])):
+            ramp[int(h["page_ids"][pg0 + (off + i) // PS]), (off + i) % PS] = 0.5 + (pos0 + i) / 60.0
+    kv[:, 0] *= ramp.to(DEV)[:, None, :, None]
+    kv = kv.bfloat16()
+    q = torch.randn(T, Hkv * G, D, device=DEV, generator=g).abs().bfloat16()
+    cos, sin = ops.build_cos_sin(D, 10000.0, 2048, device=DEV)
+    out = ops.attention(q, kv, meta, cos, sin, D ** -0.5, False)
+    ref = ops.attention_ref(q.cpu().float(), kv.cpu().float(), meta, cos.cpu(), sin.cpu(), D ** -0.5, False)
+    torch.testing.assert_close(out.float().cpu(), ref.float(), atol=3e-2, rtol=3e-2)
 
 
 def _prefill_pages256(G, splits):
