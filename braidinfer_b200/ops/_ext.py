@@ -21,7 +21,7 @@ _NOT_LAUNCHES = frozenset({
     "span_trace", "span_names", "gemm_set_trace", "attn_set_trace", "gemm_force_bn", "gemm_force_splits",
     "gemm_check_error", "gemm_prefetch_next", "comm_alloc", "comm_open", "comm_close", "comm_free",
     "comm_tensor", "tp_sample_record_bytes", "attn_select_prefill_tc",
-    "attn_prefill_tile_rows", "attn_set_exp2_poly"})
+    "attn_prefill_tile_rows", "attn_set_exp2_poly", "attn_tc_set_trace"})
 
 
 class _Counted:

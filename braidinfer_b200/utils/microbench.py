@@ -2,7 +2,7 @@
 
     python -m braidinfer_b200.utils.microbench gemm M N K [--epi 0|1] [--graph] [--rms] [--splits S | --sweep-splits]
     python -m braidinfer_b200.utils.microbench attn-decode B L HQ HKV [--splits S]
-    python -m braidinfer_b200.utils.microbench attn-prefill L HQ HKV [--batch B] [--ctx C] [--head-dim D] [--splits S]
+    python -m braidinfer_b200.utils.microbench attn-prefill L HQ HKV [--batch B] [--ctx C] [--head-dim D] [--splits S] [--trace]
     python -m braidinfer_b200.utils.microbench decode-step MODEL B PROMPT_LEN
     [torchrun --nproc-per-node N -m] braidinfer_b200.utils.microbench decode-trace MODEL B PROMPT_LEN [--out F]
     torchrun --nproc-per-node N -m braidinfer_b200.utils.microbench tp-gemm [--tokens-decode 8] ...
@@ -116,7 +116,7 @@ def bench_attn_decode(B: int, L: int, Hq: int, Hkv: int, splits: int = 0, D: int
 
 
 def bench_attn_prefill(L: int, Hq: int, Hkv: int, B: int = 1, D: int = 128, ctx: int = 0,
-                       splits: int = 0, graph: bool = False) -> dict:
+                       splits: int = 0, graph: bool = False, trace: bool = False) -> dict:
     """Causal prefill of L query tokens per sequence; with ``ctx`` the queries
     follow a cached segment of ctx keys (a query over cached chunks)."""
     from .. import ops
@@ -145,8 +145,54 @@ def bench_attn_prefill(L: int, Hq: int, Hkv: int, B: int = 1, D: int = 128, ctx:
     us = (_graph_time if graph else _eager_time)(
         lambda i: ops.attention(qs[i % nc], kvs[i % nc], meta, cos, sin, D ** -0.5))
     flops = B * 4 * (L * L / 2 + L * ctx) * Hq * D
-    return {"kernel": "attn_prefill", "L": L, "ctx": ctx, "Hq": Hq, "Hkv": Hkv, "D": D, "B": B, "us": round(us, 1),
-            "TFLOPS_causal": round(flops / us / 1e6, 1)}
+    res = {"kernel": "attn_prefill", "L": L, "ctx": ctx, "Hq": Hq, "Hkv": Hkv, "D": D, "B": B, "us": round(us, 1),
+           "TFLOPS_causal": round(flops / us / 1e6, 1)}
+    if trace:
+        res["tc_trace"] = _tc_trace(lambda: ops.attention(qs[0], kvs[0], meta, cos, sin, D ** -0.5),
+                                    -(-L * (Hq // Hkv) // 256) * B * Hkv * 32)
+    return res
+
+
+def _tc_trace(run, max_ctas: int) -> dict:
+    """One launch of the tcgen05 prefill kernel with its per-tile timestamps:
+    softmax time per key tile (S ready -> P handed over), MMA turnaround (P
+    handed over -> next S ready), first S after the CTA start, CTA length."""
+    import numpy as np
+
+    from ..ops._ext import ext
+
+    buf = torch.zeros(max_ctas * 128, dtype=torch.int64, device="cuda")
+    ext().attn_tc_set_trace(buf)
+    try:
+        run()
+        torch.cuda.synchronize()
+    finally:
+        ext().attn_tc_set_trace(torch.empty(0, dtype=torch.int64, device="cuda"))
+    t = buf.view(-1, 2, 64).cpu().numpy().astype(np.float64)
+    t = t[t[:, 0, 62] > 0]
+    soft, turn, first, cta, setup, kfirst, qbuilt, s0 = [], [], [], [], [], [], [], []
+    for c in t:
+        t0 = c[0, 62]
+        cta.append((c[0, 63] - t0) / 1e3)
+        setup.append((c[1, 62] - t0) / 1e3)
+        if c[1, 63] > 0:
+            kfirst.append((c[1, 63] - t0) / 1e3)
+        if c[0, 61] > 0:
+            s0.append((c[0, 61] - t0) / 1e3)
+        for q in range(2):
+            if c[q, 60] > 0:
+                qbuilt.append((c[q, 60] - t0) / 1e3)
+            s, pp = c[q, 0:60:2], c[q, 1:60:2]
+            n = int(np.count_nonzero(s))
+            if n == 0:
+                continue
+            first.append((s[0] - c[0, 62]) / 1e3)
+            soft += list((pp[:n] - s[:n]) / 1e3)
+            turn += list((s[1:n] - pp[:n - 1]) / 1e3)
+    q = lambda v: {"median": round(float(np.median(v)), 3), "mean": round(float(np.mean(v)), 3)} if v else None  # noqa: E731
+    return {"ctas": int(len(t)), "softmax_us": q(soft), "turnaround_us": q(turn), "first_s_us": q(first),
+            "cta_us": q(cta), "setup_us": q(setup), "first_k_issued_us": q(kfirst), "q_built_us": q(qbuilt),
+            "s0_issued_us": q(s0)}
 
 
 def decode_step(model: str, B: int, plen: int) -> None:
@@ -548,6 +594,7 @@ def main(argv=None) -> None:
     p.add_argument("--head-dim", type=int, default=128)
     p.add_argument("--splits", type=int, default=0, help="force key splits (0: automatic)")
     p.add_argument("--graph", action="store_true", help="time 20 launches replayed from a CUDA graph")
+    p.add_argument("--trace", action="store_true", help="tcgen05 kernel: per-tile softmax / MMA turnaround times")
     tg = sub.add_parser("tp-gemm", help="row-parallel GEMM + collective, under torchrun (one rank per GPU)")
     tg.add_argument("--tokens-decode", type=int, default=8)
     tg.add_argument("--tokens-prefill", type=int, default=4096)
@@ -589,7 +636,7 @@ def main(argv=None) -> None:
         print(json.dumps(bench_attn_decode(args.B, args.L, args.Hq, args.Hkv, args.splits)))
     elif args.cmd == "attn-prefill":
         print(json.dumps(bench_attn_prefill(args.L, args.Hq, args.Hkv, args.batch, args.head_dim, args.ctx,
-                                            args.splits, args.graph)))
+                                            args.splits, args.graph, args.trace)))
     else:
         decode_step(args.model, args.B, args.plen)
         print("decode step done")

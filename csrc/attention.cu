@@ -1028,6 +1028,13 @@ static unsigned long long* g_attn_trace = nullptr;
 void attn_set_trace(torch::Tensor buf) {
   g_attn_trace = buf.defined() && buf.numel() ? reinterpret_cast<unsigned long long*>(buf.data_ptr<int64_t>()) : nullptr;
 }
+// Profiling: per-tile softmax timestamps of subsequent tcgen05 prefill launches
+// (int64 [128 * CTAs]; attention_tc.cu documents the layout).
+static unsigned long long* g_attn_tc_trace = nullptr;
+void attn_tc_set_trace(torch::Tensor buf) {
+  g_attn_tc_trace =
+      buf.defined() && buf.numel() ? reinterpret_cast<unsigned long long*>(buf.data_ptr<int64_t>()) : nullptr;
+}
 
 int gemm_num_sms();
 unsigned long long* next_span(const char* name);
@@ -1050,14 +1057,16 @@ static int* attn_counters(int dev, size_t n) {
   return e.first;
 }
 
-bool attn_prefill_tc_enabled(int D);
+bool attn_prefill_tc_use(int D, int64_t rows);
+bool attn_shared_tc_use(int D);
 int attn_prefill_tc_rows();
+int attn_prefill_tc_min_rows();
 void launch_attn_prefill_tc(const AttnParams& p, int num_seqs, int max_q_len, int64_t P, cudaStream_t st);
 
 template <int D>
 static void launch_attn(AttnParams& p, int num_seqs, int max_q_len, bool decode, int T, int64_t P,
                         cudaStream_t st) {
-  if (!decode && attn_prefill_tc_enabled(D)) {  // tcgen05 prefill (attention_tc.cu)
+  if (!decode && p.use_tc) {  // tcgen05 prefill (attention_tc.cu)
     launch_attn_prefill_tc(p, num_seqs, max_q_len, P, st);
     return;
   }
@@ -1163,7 +1172,17 @@ void attention(torch::Tensor out, torch::Tensor q, torch::Tensor kv, torch::Tens
   } else {
     // Prefill: split the keys when the q tiles alone leave SMs idle (a short
     // query over long cached chunks); each split keeps >= 2 key tiles.
-    const int tile_rows = attn_prefill_tc_enabled(D) ? attn_prefill_tc_rows() : 64;
+    const int sms_ = gemm_num_sms();
+    int tile_rows = 64;
+    p.use_tc = attn_prefill_tc_use(D, (int64_t)T * G) ? 1 : 0;
+    if (p.use_tc) {
+      // tcgen05 kernel: 256-row CTAs (two Q tiles), or 128-row CTAs when the
+      // 256-row work units would fill less than half of the SMs
+      const int64_t w256 = (int64_t)((max_q_len * G + attn_prefill_tc_rows() - 1) / attn_prefill_tc_rows()) *
+                           num_seqs * Hkv;
+      tile_rows = w256 * 2 <= sms_ ? attn_prefill_tc_min_rows() : attn_prefill_tc_rows();
+    }
+    p.cta_rows = tile_rows;
     const int qt = (int)((max_q_len * G + tile_rows - 1) / tile_rows);
     const int64_t work = (int64_t)qt * num_seqs * Hkv;
     static const int forced = [] {  // tuning knob: BRAID_PREFILL_SPLITS=n
@@ -1172,13 +1191,30 @@ void attention(torch::Tensor out, torch::Tensor q, torch::Tensor kv, torch::Tens
     }();
     int ns = 1;
     const int sms = gemm_num_sms();
-    if (work < sms) ns = (int)std::min<int64_t>({(2 * sms + work - 1) / work, 32, std::max<int64_t>(1, max_kv_len / 128)});
+    if (work < sms && p.use_tc) {
+      // one CTA per SM: pick the split count with the fewest (waves x key
+      // tiles per CTA, plus about two tiles of fixed cost per CTA), plus the
+      // merge, whose last CTA reads every split's 256-row partial (about one
+      // tile's time per split)
+      const int64_t kvt = std::max<int64_t>(1, (max_kv_len + 127) / 128);
+      int64_t best = INT64_MAX;
+      for (int n = 1; n <= 32 && n <= kvt; ++n) {
+        const int64_t est = ((work * n + sms - 1) / sms) * ((kvt + n - 1) / n + 2) + (n > 1 ? n : 0);
+        if (est < best) {
+          best = est;
+          ns = n;
+        }
+      }
+    } else if (work < sms) {
+      ns = (int)std::min<int64_t>({(2 * sms + work - 1) / work, 32, std::max<int64_t>(1, max_kv_len / 128)});
+    }
     if (num_splits > 1) ns = (int)std::min<int64_t>(num_splits, 32);
     if (forced > 0) ns = std::min(forced, 32);
     p.num_splits = std::max(1, ns);
     n_counters = (size_t)qt * num_seqs * Hkv;
   }
   p.trace = g_attn_trace;
+  p.tc_trace = g_attn_tc_trace;
   // Decode K/V are read once per step (shared chunk pages by CTAs running at
   // the same time): evict-first keeps them from pushing out other lines.
   // Tuning knob: BRAID_KV_EVICT_FIRST=0 uses the default L2 policy.
@@ -1231,6 +1267,7 @@ void attention(torch::Tensor out, torch::Tensor q, torch::Tensor kv, torch::Tens
     a.split_base = 0;
     a.split_stride = S_tot;
     a.partial_only = 1;
+    a.use_tc = attn_shared_tc_use(D) ? 1 : 0;
     a.span = next_span("attn_shared_prefix");
     run(a, grp_qo_indptr->numel() - 1, std::max<int64_t>(1, grp_max_q), false);
     p.split_base = S_sh;

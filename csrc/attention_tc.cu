@@ -128,38 +128,58 @@ BRAID_DEVICE bool tc_next(const AttnParams& p, const TcRange& rg, TcWalk& w, boo
 }
 
 // Rotated query row r (token tok, head) for a segment with RoPE delta `delta`,
-// written into the K-major swizzled Q tile; rows past the tile are zero.
+// written into the K-major swizzled Q tile; rows past the tile are zero.  All
+// 16 loads of the row are issued first and the cos/sin rows follow in two
+// halves of 16 float4 loads each (about three memory round trips per row).
 BRAID_DEVICE void tc_build_q_row(const AttnParams& p, uint8_t* qs, int r, bool live, int tok, int head, int rpos,
                                  int delta) {
   const __nv_bfloat16* qp = p.q + ((size_t)tok * p.Hq + head) * TC_D;
-  int pos = rpos - delta;
-  pos = pos < 0 ? 0 : (pos >= p.rope_len ? p.rope_len - 1 : pos);
+  uint4 qa[8], qb[8];
 #pragma unroll
   for (int c = 0; c < 8; ++c) {
-    uint4 o1 = make_uint4(0, 0, 0, 0), o2 = make_uint4(0, 0, 0, 0);
-    if (live) {
-      const uint4 a4 = *reinterpret_cast<const uint4*>(qp + c * 8);
-      const uint4 b4 = *reinterpret_cast<const uint4*>(qp + 64 + c * 8);
-      if (p.use_rope) {
-        const float* cp = p.cos + (size_t)pos * 64 + c * 8;
-        const float* sp = p.sin + (size_t)pos * 64 + c * 8;
-        const __nv_bfloat16* a = reinterpret_cast<const __nv_bfloat16*>(&a4);
-        const __nv_bfloat16* bb = reinterpret_cast<const __nv_bfloat16*>(&b4);
+    qa[c] = live ? __ldg(reinterpret_cast<const uint4*>(qp + c * 8)) : make_uint4(0, 0, 0, 0);
+    qb[c] = live ? __ldg(reinterpret_cast<const uint4*>(qp + 64 + c * 8)) : make_uint4(0, 0, 0, 0);
+  }
+  if (live && p.use_rope) {
+    int pos = rpos - delta;
+    pos = pos < 0 ? 0 : (pos >= p.rope_len ? p.rope_len - 1 : pos);
+    const float4* cp = reinterpret_cast<const float4*>(p.cos + (size_t)pos * 64);
+    const float4* sp = reinterpret_cast<const float4*>(p.sin + (size_t)pos * 64);
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      float4 cs[8], sn[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        cs[u] = __ldg(cp + hf * 8 + u);
+        sn[u] = __ldg(sp + hf * 8 + u);
+      }
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        const int c = hf * 4 + cc;
+        const float cf[8] = {cs[2 * cc].x, cs[2 * cc].y, cs[2 * cc].z, cs[2 * cc].w,
+                             cs[2 * cc + 1].x, cs[2 * cc + 1].y, cs[2 * cc + 1].z, cs[2 * cc + 1].w};
+        const float sf[8] = {sn[2 * cc].x, sn[2 * cc].y, sn[2 * cc].z, sn[2 * cc].w,
+                             sn[2 * cc + 1].x, sn[2 * cc + 1].y, sn[2 * cc + 1].z, sn[2 * cc + 1].w};
+        const __nv_bfloat16* a = reinterpret_cast<const __nv_bfloat16*>(&qa[c]);
+        const __nv_bfloat16* bb = reinterpret_cast<const __nv_bfloat16*>(&qb[c]);
+        uint4 o1, o2;
         __nv_bfloat16* y1 = reinterpret_cast<__nv_bfloat16*>(&o1);
         __nv_bfloat16* y2 = reinterpret_cast<__nv_bfloat16*>(&o2);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          const float x1 = bf2f(a[e]), x2 = bf2f(bb[e]), cs = cp[e], sn = sp[e];
-          y1[e] = f2bf(x1 * cs - x2 * sn);
-          y2[e] = f2bf(x2 * cs + x1 * sn);
+          const float x1 = bf2f(a[e]), x2 = bf2f(bb[e]);
+          y1[e] = f2bf(x1 * cf[e] - x2 * sf[e]);
+          y2[e] = f2bf(x2 * cf[e] + x1 * sf[e]);
         }
-      } else {
-        o1 = a4;
-        o2 = b4;
+        qa[c] = o1;
+        qb[c] = o2;
       }
     }
-    *reinterpret_cast<uint4*>(qs + tc_off(r, c)) = o1;
-    *reinterpret_cast<uint4*>(qs + tc_off(r, c + 8)) = o2;
+  }
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    *reinterpret_cast<uint4*>(qs + tc_off(r, c)) = qa[c];
+    *reinterpret_cast<uint4*>(qs + tc_off(r, c + 8)) = qb[c];
   }
 }
 
@@ -222,12 +242,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_prefill_tc_kernel(const __
   const int b = (lin % yz) % gridDim.y, z = (lin % yz) / gridDim.y;
   const int kh = z / S, split = z % S;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // profiling (p.tc_trace): per CTA 128 timestamps; Q tile t at 64 t:
+  // [2j] S(t, j) ready, [2j + 1] P(t, j) handed to the MMA warp (j < 30),
+  // [60] Q(t) built; [61] S(0, 0) issued, [62] CTA start, [63] end,
+  // [126] barriers and TMEM set up, [127] first K tile issued
+  unsigned long long* trc = p.tc_trace ? p.tc_trace + (size_t)lin * 128 : nullptr;
+  if (trc != nullptr && threadIdx.x == 0) trc[62] = globaltimer_ns();
   const int G = p.G;
   const int t0 = p.qo_indptr[b], nt = p.qo_indptr[b + 1] - t0;
   const int rows = nt * G;
-  const int row0 = qtile * TC_CTA_ROWS;
+  const int cta_rows = p.cta_rows == TC_ROWS ? TC_ROWS : TC_CTA_ROWS;
+  const int row0 = qtile * cta_rows;
   if (row0 >= rows) return;
-  const int nrows = min(TC_CTA_ROWS, rows - row0);
+  const int nrows = min(cta_rows, rows - row0);
   const int nq = nrows > TC_ROWS ? 2 : 1;  // Q tiles with live rows (CTA-uniform)
   // largest position among the CTA's rows (rows of a shared-prefix group are not ordered)
   TcRange rg;
@@ -275,6 +302,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_prefill_tc_kernel(const __
   tc_fence_after();
   const uint32_t tmem = bar.tmem;
   pdl_trigger();
+  if (trc != nullptr && threadIdx.x == 0) trc[126] = globaltimer_ns();
 
   TcWalk w{s0, s1, 0, 0, 0, 0, 0};
   bool more = tc_settle(p, rg, w);
@@ -283,6 +311,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_prefill_tc_kernel(const __
     // ------------------------------------------------------------ producer
     if (lane == 0 && more) {
       pdl_wait();
+      span_waited(p.span);
       int j = 0, kiss = 0, viss = 0;
       while (more) {
         const int st = j % TC_STAGES;
@@ -306,6 +335,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_prefill_tc_kernel(const __
 #pragma unroll
           for (int h = 0; h < 2; ++h)
             tma_load_2d(kst + st * TC_TILE + h * TC_HALF + q * BR * 128, &tmkv, &bar.kfull[st], h * 64, rk[q]);
+        if (trc != nullptr && j == 0) trc[127] = globaltimer_ns();
         ++kiss;
         if (j >= TC_STAGES && !mbar_wait(&bar.vempty[st], ph)) {
           s_abort = 1;
@@ -357,6 +387,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_prefill_tc_kernel(const __
       ok = ok && mbar_wait(&bar.kfull[0], 0);
       if (ok) {
         tc_fence_after();
+        if (trc != nullptr) trc[61] = globaltimer_ns();
         for (int t = 0; t < nq; ++t) {
           issue_s(t, 0);
           tc_commit(&bar.sfull[t]);
@@ -419,10 +450,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_prefill_tc_kernel(const __
       float m_run = -INFINITY, l_run = 0.f;
       int j = 0;
       if (more) {
+        const int delta0 = p.seg_delta[w.s];
         pdl_wait();
-        tc_build_q_row(p, qs, r, live, tok, head, rpos, p.seg_delta[w.s]);
+        tc_build_q_row(p, qs, r, live, tok, head, rpos, delta0);
         fence_proxy_async_smem();
         mbar_arrive(&bar.pready[t]);
+        if (trc != nullptr && r == 0) trc[t * 64 + 60] = globaltimer_ns();
       }
       while (more) {
         const int pos0 = p.seg_pos0[w.s], j0 = w.sl - w.off, lo = w.lo, hi = w.hi;
@@ -431,6 +464,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_prefill_tc_kernel(const __
           break;
         }
         tc_fence_after();
+        if (trc != nullptr && r == 0 && j < 30) trc[t * 64 + 2 * j] = globaltimer_ns();
         uint32_t sr[TC_KEYS];
 #pragma unroll
         for (int c = 0; c < TC_KEYS / 32; ++c) tmem_ld32(tS + c * 32, sr + c * 32);
@@ -499,6 +533,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_prefill_tc_kernel(const __
         fence_proxy_async_smem();
         tc_fence_before();
         mbar_arrive(&bar.pready[t]);
+        if (trc != nullptr && r == 0 && j < 30) trc[t * 64 + 2 * j + 1] = globaltimer_ns();
         ++j;
       }
       const bool have = j > 0 && !s_abort;
@@ -566,18 +601,28 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_prefill_tc_kernel(const __
           }
           const float winv = sum > 0.f ? 1.f / sum : 0.f;
           __nv_bfloat16* o = p.out + ((size_t)tok * p.Hq + head) * TC_D;
-          for (int d = 0; d < TC_D; d += 4) {
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int q = 0; q < S; ++q) {
-              if (wq[q] == 0.f) continue;
-              const float4 v = __ldcg(reinterpret_cast<const float4*>(p.part_o + (base + q) * TC_D + d));
-              acc.x += wq[q] * v.x;
-              acc.y += wq[q] * v.y;
-              acc.z += wq[q] * v.z;
-              acc.w += wq[q] * v.w;
+          for (int d = 0; d < TC_D; d += 8) {
+            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            for (int q0 = 0; q0 < S; q0 += 8) {
+              // eight splits' partials of these 8 dims in flight before any is summed
+              float4 v[8][2];
+#pragma unroll
+              for (int u = 0; u < 8; ++u) {
+                const bool use = q0 + u < S;
+                const float4* src = reinterpret_cast<const float4*>(p.part_o + (base + q0 + u) * TC_D + d);
+                v[u][0] = use ? __ldcg(src) : make_float4(0.f, 0.f, 0.f, 0.f);
+                v[u][1] = use ? __ldcg(src + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
+              }
+#pragma unroll
+              for (int u = 0; u < 8; ++u) {
+                const float wu = q0 + u < S ? wq[q0 + u] : 0.f;
+                acc[0] += wu * v[u][0].x; acc[1] += wu * v[u][0].y; acc[2] += wu * v[u][0].z; acc[3] += wu * v[u][0].w;
+                acc[4] += wu * v[u][1].x; acc[5] += wu * v[u][1].y; acc[6] += wu * v[u][1].z; acc[7] += wu * v[u][1].w;
+              }
             }
-            *reinterpret_cast<__nv_bfloat162*>(o + d) = __floats2bfloat162_rn(acc.x * winv, acc.y * winv);
-            *reinterpret_cast<__nv_bfloat162*>(o + d + 2) = __floats2bfloat162_rn(acc.z * winv, acc.w * winv);
+            *reinterpret_cast<uint4*>(o + d) =
+                make_uint4(pack_bf16(acc[0] * winv, acc[1] * winv), pack_bf16(acc[2] * winv, acc[3] * winv),
+                           pack_bf16(acc[4] * winv, acc[5] * winv), pack_bf16(acc[6] * winv, acc[7] * winv));
           }
         }
       }
@@ -589,6 +634,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_prefill_tc_kernel(const __
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+  if (trc != nullptr && threadIdx.x == 0) trc[63] = globaltimer_ns();
   if (threadIdx.x == 0) span_end(p.span);
 }
 
@@ -598,36 +644,54 @@ namespace braid {
 
 CUtensorMap make_tmap(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows);
 
-// Prefill kernel choice for head_dim 128: -1 follows BRAID_ATTN_TC (1 selects
-// this kernel, anything else the mma.sync kernel of attention.cu); 0 / 1 set by
-// attn_select_prefill_tc.
+// Prefill kernel choice for head_dim 128.  Mode 1 always takes this kernel,
+// 0 the mma.sync kernel of attention.cu, -1 (auto) this kernel for prefill
+// calls of at least 1024 (token, head) rows: on B200 it runs 2.2-2.9x faster
+// there (2048 causal: 59 vs 170 us; 256 queries over 7000 cached keys: 79 vs
+// 174 us), while for a short query over a long cached context and for the
+// shared-prefix pass of a grouped decode step (256 rows and fewer) the
+// mma.sync kernel's 64-row tiles spread the keys over more SMs (64 queries
+// over 3200 keys: 35 vs 50 us).  Mode: attn_select_prefill_tc, else
+// BRAID_ATTN_TC (1 / 0), else auto.
 static int g_attn_tc = -1;
 
 void attn_select_prefill_tc(int64_t mode) { g_attn_tc = mode < 0 ? -1 : (mode ? 1 : 0); }
+
+static int attn_tc_mode() {
+  static const int env_mode = [] {
+    const char* e = getenv("BRAID_ATTN_TC");
+    return e == nullptr ? -1 : (e[0] == '1' ? 1 : 0);
+  }();
+  return g_attn_tc >= 0 ? g_attn_tc : env_mode;
+}
+
+// Prefill call of `rows` (token, head) rows with head dim D.
+bool attn_prefill_tc_use(int D, int64_t rows) {
+  if (D != TC_D) return false;
+  const int m = attn_tc_mode();
+  return m == 1 || (m < 0 && rows >= 1024);
+}
+
+// Shared-prefix pass of a grouped decode step.
+bool attn_shared_tc_use(int D) { return D == TC_D && attn_tc_mode() == 1; }
 
 // Share of the tcgen05 prefill softmax exponentials computed by polynomial
 // (every n-th of a row; 0 none; -1 follows BRAID_ATTN_POLY); 256-token pages.
 static int g_attn_poly = -1;
 void attn_set_exp2_poly(int64_t n) { g_attn_poly = n < 0 ? -1 : (n == 2 || n == 4 ? (int)n : 0); }
 
-bool attn_prefill_tc_enabled(int D) {
-  static const bool env_on = [] {
-    const char* e = getenv("BRAID_ATTN_TC");
-    return e && e[0] == '1';
-  }();
-  const bool on = g_attn_tc < 0 ? env_on : g_attn_tc == 1;
-  return on && D == TC_D;
-}
-
 int attn_prefill_tc_rows() { return TC_CTA_ROWS; }
+int attn_prefill_tc_min_rows() { return TC_ROWS; }
 
-// Query rows per CTA of the prefill kernel that serves head_dim D (the
-// tcgen05 kernel holds one CTA per SM, the mma.sync kernel two).
-int64_t attn_prefill_tile_rows(int64_t D) { return attn_prefill_tc_enabled((int)D) ? TC_CTA_ROWS : 64; }
+// Query rows per CTA of the kernel that runs the shared-prefix pass of a
+// grouped decode step for head_dim D (the tcgen05 kernel holds one CTA per
+// SM, the mma.sync kernel two).
+int64_t attn_prefill_tile_rows(int64_t D) { return attn_shared_tc_use((int)D) ? TC_CTA_ROWS : 64; }
 
 void launch_attn_prefill_tc(const AttnParams& p, int num_seqs, int max_q_len, int64_t P, cudaStream_t st) {
   const int64_t rows = P * 2 * p.Hkv * p.PS;  // the layer pool as rows of head_dim elements
-  const int qt = (max_q_len * p.G + TC_CTA_ROWS - 1) / TC_CTA_ROWS;
+  const int cr = p.cta_rows == TC_ROWS ? TC_ROWS : TC_CTA_ROWS;
+  const int qt = (max_q_len * p.G + cr - 1) / cr;
   const dim3 grid(qt, num_seqs, p.Hkv * p.num_splits);
   static const int env_poly = [] {  // tuning knob: BRAID_ATTN_POLY = 0, 2 or 4
     const char* e = getenv("BRAID_ATTN_POLY");

@@ -33,9 +33,12 @@ struct AttnParams {
   float* part_lse;  // [T, Hq, splits]
   int* counters;    // [T * Hkv] split arrival counters, kept at zero between launches
   unsigned long long* trace;  // optional per-CTA phase timestamps (profiling)
+  unsigned long long* tc_trace;  // tcgen05 prefill: 128 timestamps per CTA (profiling)
   unsigned long long* span;   // optional launch span (profiling)
   PrefetchArgs pf;            // decode: the next GEMM's weight to pull into L2 (tensor map tmP)
-  int pf_early;               // decode: issue that prefetch with the first K/V tiles (else after the last)
+  int pf_early;
+  int cta_rows;               // tcgen05 prefill: query rows per CTA (256 = two Q tiles, or 128)
+  int use_tc;                 // prefill launch: the tcgen05 kernel (attention_tc.cu), else mma.sync               // decode: issue that prefetch with the first K/V tiles (else after the last)
   int kv_evict_first;         // decode: read K/V with the evict-first L2 policy
   // Shared-prefix decode (segments common to a group of sequences are read
   // once for all of them): partials live at split index split_base + split

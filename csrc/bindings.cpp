@@ -47,6 +47,7 @@ void attention(torch::Tensor out, torch::Tensor q, torch::Tensor kv, torch::Tens
                c10::optional<torch::Tensor> grp_qo_indptr, c10::optional<torch::Tensor> grp_seg_indptr,
                c10::optional<torch::Tensor> seq_nsh, int64_t shared_splits, int64_t grp_max_q);
 void attn_set_trace(torch::Tensor buf);
+void attn_tc_set_trace(torch::Tensor buf);
 void attn_select_prefill_tc(int64_t mode);
 int64_t attn_prefill_tile_rows(int64_t D);
 void attn_set_exp2_poly(int64_t n);
@@ -117,6 +118,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "tcgen05 prefill softmax: every n-th exponential by polynomial on the FMA pipe (n = 0, 2, 4; -1: BRAID_ATTN_POLY)");
   m.def("attn_select_prefill_tc", &braid::attn_select_prefill_tc,
         "prefill attention for head_dim 128: 1 tcgen05 kernel, 0 mma.sync kernel, -1 BRAID_ATTN_TC");
+  m.def("attn_tc_set_trace", &braid::attn_tc_set_trace,
+        "profiling: per-tile softmax timestamps of later tcgen05 prefill attention (int64, 128 per CTA)");
   m.def("attn_set_trace", &braid::attn_set_trace, "profiling: per-CTA phase timestamps of later decode attention");
   m.def("rms_norm", &braid::rms_norm);
   m.def("add_rms_norm", &braid::add_rms_norm);

@@ -276,6 +276,7 @@ __global__ void __launch_bounds__(SNT) tp_sample_kernel(
   __shared__ int s_cid[8 * TPS_KC];
   if (threadIdx.x == 0) span_start(span);
   pdl_wait();
+  if (threadIdx.x == 0) span_waited(span);
   const int row = blockIdx.x, B = gridDim.x;
   const uint64_t epoch = epoch_state[0];
   const uint64_t expected = epoch_state[1] + (uint64_t)B;

@@ -20,8 +20,9 @@ def _check_err():
 
 @pytest.fixture(params=[1, 0], ids=["tc", "mma"])
 def prefill_kernel(request):
-    """Runs the test on each prefill attention kernel for head_dim 128: the
-    tcgen05 kernel (attention_tc.cu) and the mma.sync kernel (attention.cu)."""
+    """Runs the test on each prefill attention kernel for head_dim 128, forced
+    for every prefill call (and the shared-prefix pass): the tcgen05 kernel
+    (attention_tc.cu) and the mma.sync kernel (attention.cu)."""
     _ext().attn_select_prefill_tc(request.param)
     yield request.param
     _ext().attn_select_prefill_tc(-1)
