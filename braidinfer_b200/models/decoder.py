@@ -38,6 +38,8 @@ from ..parallel.state import TPState
 PREFETCH_ALL = os.environ.get("BRAID_PREFETCH_ALL", "0") == "1"
 # decode attention pulls the o_proj weight into L2 while it streams K/V
 PREFETCH_ATTN = os.environ.get("BRAID_PREFETCH_ATTN", "0") == "1"
+# the down-projection GEMM pulls the next layer's QKV weight into L2 (TP1)
+PREFETCH_QKV = os.environ.get("BRAID_PREFETCH_QKV", "0") == "1"
 
 
 class LayerWeights:
@@ -268,7 +270,8 @@ class DecoderLM:
             residual = self._row_parallel(o, w.o_w, residual, w.gu_w, gu_done)
             nxt(w.down_w, T)
             g = ops.linear_swiglu(residual, w.gu_w, rms_eps=eps)
-            residual = self._row_parallel(g, w.down_w, residual, following)
+            residual = self._row_parallel(g, w.down_w, residual, following,
+                                          pull_next=PREFETCH_QKV and i + 1 < len(self.layers))
         return residual
 
     def _forward_sp(self, fc, input_ids, positions, slot_mapping, meta, kv_cache, workspace) -> torch.Tensor:
@@ -301,12 +304,15 @@ class DecoderLM:
         return G.clone()
 
     def _row_parallel(self, x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor,
-                      w_next: Optional[torch.Tensor] = None, skip: int = 0) -> torch.Tensor:
+                      w_next: Optional[torch.Tensor] = None, skip: int = 0, pull_next: bool = False) -> torch.Tensor:
         """``residual += x @ w.T`` summed over tensor-parallel ranks; the
         GEMM (and the reduce kernel after it) prefetch ``w_next`` into L2,
-        past the ``skip`` leading K-blocks per slice already requested."""
+        past the ``skip`` leading K-blocks per slice already requested
+        (``pull_next``: the single-GPU GEMM prefetches it as well)."""
         T = x.shape[0]
         done = ops.prefetch_next(w_next, T, skip) if PREFETCH_ALL else skip
+        if pull_next and not PREFETCH_ALL and self.tp.size == 1:
+            ops.prefetch_next(w_next, T)
         if self.tp.size == 1:
             return ops.linear(x, w, residual=residual, out=residual)
         fc = comm.get_fused_comm()
