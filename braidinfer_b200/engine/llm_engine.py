@@ -24,6 +24,7 @@ from ..errors import ConfigurationError
 from ..parallel.state import get_tp, init_tp
 from ..sampling_params import SamplingParams
 from ..utils.logging import get_logger
+from ..utils.tracing import nvtx_range
 from .chat_format import ChatFormat
 from .metrics import MetricsCollector
 from .model_runner import ModelRunner
@@ -165,7 +166,8 @@ class LLMEngine:
             return []
         t0 = time.perf_counter()
         ntok = sum(max(1, s.num_tokens - s.num_cached_tokens) for s in seqs)
-        token_ids = self.model_runner.run(seqs, is_prefill)
+        with nvtx_range(f"{'prefill' if is_prefill else 'decode'} b={len(seqs)} t={ntok}"):
+            token_ids = self.model_runner.run(seqs, is_prefill)
         now = time.perf_counter()
         dt = now - t0
         self._timing_stats.append(dt)

@@ -27,6 +27,7 @@ from ..config import Config
 from ..models import build_model
 from ..parallel.state import TPState
 from ..utils.logging import get_logger
+from ..utils.tracing import nvtx_range
 from .batch import FwdItem, Plan, build_plan, find_shared_group, make_meta, pack, unpack
 from .page_manager import PageManager
 from .sequence import Sequence
@@ -177,7 +178,8 @@ class ModelRunner:
         sh = self._shared_splits(plan.num_seqs, ns) if group is not None and group[0] > 0 else 0
         meta = make_meta(views, plan, ns, shared_splits=sh)
         kv = self.page_manager.kv_cache
-        h = self.model.forward(views["input_ids"], views["positions"], views["slots"], meta, kv)
+        with nvtx_range(f"forward t={plan.sizes['input_ids']}"):
+            h = self.model.forward(views["input_ids"], views["positions"], views["slots"], meta, kv)
         rows = h.index_select(0, views["logits_idx"].long()) if plan.sizes["logits_idx"] else h[:0]
         return self.model.final_hidden(rows)
 
@@ -191,6 +193,10 @@ class ModelRunner:
         return items
 
     def sample(self, hn: torch.Tensor, seqs: List[Sequence]) -> torch.Tensor:
+        with nvtx_range("sample"):
+            return self._sample(hn, seqs)
+
+    def _sample(self, hn: torch.Tensor, seqs: List[Sequence]) -> torch.Tensor:
         logits = self.model.compute_logits(hn)
         if self.capture_logits is not None:
             self.capture_logits.append(logits.float().cpu())
@@ -450,6 +456,10 @@ class ModelRunner:
         return self._replay(g, plan, [seq], 1)
 
     def _replay(self, g: _GraphSlot, plan, seqs: List[Sequence], B: int) -> List[int]:
+        with nvtx_range(f"graph replay b={B}"):
+            return self._replay_graph(g, plan, seqs, B)
+
+    def _replay_graph(self, g: _GraphSlot, plan, seqs: List[Sequence], B: int) -> List[int]:
         # Persistent pinned staging: the previous step's copies completed at its
         # token read-back, so the buffers are free to overwrite.
         if g.pin_meta is None:
