@@ -8,6 +8,8 @@ of the tests (and the only way the engine runs without a GPU).
 """
 from __future__ import annotations
 
+import os
+
 from ..errors import KernelUnavailableError
 
 _C = None
@@ -21,7 +23,8 @@ _NOT_LAUNCHES = frozenset({
     "span_trace", "span_names", "gemm_set_trace", "attn_set_trace", "gemm_force_bn", "gemm_force_splits",
     "gemm_check_error", "gemm_prefetch_next", "comm_alloc", "comm_open", "comm_close", "comm_free",
     "comm_tensor", "tp_sample_record_bytes", "attn_select_prefill_tc",
-    "attn_prefill_tile_rows", "attn_set_exp2_poly", "attn_tc_set_trace"})
+    "attn_prefill_tile_rows", "attn_set_exp2_poly", "attn_tc_set_trace",
+    "bounds_check_status", "bounds_check_enabled"})
 
 
 class _Counted:
@@ -50,7 +53,10 @@ def ext():
     global _C, _err
     if _C is None:
         try:
-            from .. import _C as mod  # type: ignore[attr-defined]
+            if os.environ.get("BRAID_BOUNDS_CHECK") == "1":  # the bounds-checked build
+                from .. import _C_checked as mod  # type: ignore[attr-defined]
+            else:
+                from .. import _C as mod  # type: ignore[attr-defined]
         except Exception as e:  # pragma: no cover - depends on build
             _err = e
             raise KernelUnavailableError(

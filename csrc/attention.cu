@@ -59,14 +59,18 @@ BRAID_DEVICE void load_kv_tile(const AttnParams& p, int s, int kh, int j0, int j
   for (int i = threadIdx.x; i < KT * CH; i += blockDim.x) {
     const int row = i / CH, c = i % CH;
     const int j = j0 + row;
-    const bool ok = j < jend;
+    bool ok = j < jend;
     const __nv_bfloat16* kp = p.kv;
     const __nv_bfloat16* vp = p.kv;
     if (ok) {
       const int slot = off + j;
       const int page = pages[slot / p.PS];
-      kp = p.kv + kv_row(p, page, 0, kh, slot % p.PS, D) + c * 8;
-      vp = p.kv + kv_row(p, page, 1, kh, slot % p.PS, D) + c * 8;
+      if (BRAID_IN_BOUNDS(page >= 0 && page < p.num_pages, 4, page)) {
+        kp = p.kv + kv_row(p, page, 0, kh, slot % p.PS, D) + c * 8;
+        vp = p.kv + kv_row(p, page, 1, kh, slot % p.PS, D) + c * 8;
+      } else {
+        ok = false;  // zero-filled
+      }
     }
     cp_async16(smem_u32(ks) + swz<D>(row, c), kp, ok);
     cp_async16(smem_u32(vs) + swz<D>(row, c), vp, ok);
@@ -297,6 +301,7 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(const __grid_consta
         pc.win_page = pc.win + lane < pc.npages ? pc.pages[pc.win + lane] : 0;
       }
       const int page = __shfl_sync(0xffffffffu, pc.win_page, pidx - pc.win);
+      if (lane == 0) (void)BRAID_IN_BOUNDS(page >= 0 && page < p.num_pages, 4, page);  // TMA zero-fills outside the pool
       if (lane == 0) {
         const int row_k = ((page * 2 + 0) * p.Hkv + kh) * p.PS + slot % p.PS;
         const int row_v = row_k + p.Hkv * p.PS;
@@ -711,6 +716,7 @@ __global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const __grid_const
         pc.win_page = pc.win + lane < pc.npages ? pc.pages[pc.win + lane] : 0;
       }
       const int page = __shfl_sync(0xffffffffu, pc.win_page, pidx - pc.win);
+      if (lane == 0) (void)BRAID_IN_BOUNDS(page >= 0 && page < p.num_pages, 4, page);  // TMA zero-fills outside the pool
       if (lane == 0) {
         const int row_k = ((page * 2 + 0) * p.Hkv + kh) * p.PS + slot % p.PS;
         const int row_v = row_k + p.Hkv * p.PS;
@@ -1166,6 +1172,7 @@ void attention(torch::Tensor out, torch::Tensor q, torch::Tensor kv, torch::Tens
   p.Hkv = Hkv;
   p.G = G;
   p.PS = PS;
+  p.num_pages = (int)kv.size(0);
   size_t n_counters = (size_t)T * Hkv;
   if (decode) {
     p.num_splits = (int)std::max<int64_t>(1, num_splits);
@@ -1278,4 +1285,9 @@ void attention(torch::Tensor out, torch::Tensor q, torch::Tensor kv, torch::Tens
   run(p, num_seqs, max_q_len, decode);
 }
 
+}  // namespace braid
+
+// status word of this file's kernels (checked build; 0 otherwise)
+namespace braid {
+BRAID_BOUNDS_READER(bounds_status_attention)
 }  // namespace braid

@@ -323,6 +323,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_prefill_tc_kernel(const __
         for (int q = 0; q < TC_KEYS / BR; ++q) {
           const int slot = w.sl + q * BR;
           const int page = pages[min(slot / p.PS, npages - 1)];
+          (void)BRAID_IN_BOUNDS(page >= 0 && page < p.num_pages, 4, page);  // TMA zero-fills outside the pool
           rk[q] = ((page * 2 + 0) * p.Hkv + kh) * p.PS + slot % p.PS;
         }
         if (j >= TC_STAGES && !mbar_wait(&bar.kempty[st], ph)) {
@@ -719,4 +720,9 @@ void launch_attn_prefill_tc(const AttnParams& p, int num_seqs, int max_q_len, in
   }
 }
 
+}  // namespace braid
+
+// status word of this file's kernels (checked build; 0 otherwise)
+namespace braid {
+BRAID_BOUNDS_READER(bounds_status_attention_tc)
 }  // namespace braid

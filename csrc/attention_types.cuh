@@ -28,6 +28,7 @@ struct AttnParams {
   int use_rope;
   int rope_len;
   int Hq, Hkv, G, PS;
+  int num_pages;    // pages of the KV pool (checked build)
   int num_splits;
   float* part_o;    // [T, Hq, splits, D]
   float* part_lse;  // [T, Hq, splits]

@@ -11,6 +11,31 @@ void gemm_qkv(torch::Tensor q_out, torch::Tensor x, torch::Tensor w, c10::option
               torch::Tensor cos, torch::Tensor sin, int64_t Hq, int64_t Hkv, int64_t D, bool use_rope,
               c10::optional<torch::Tensor> rs_vec, c10::optional<torch::Tensor> sp);
 void row_rstd(torch::Tensor x, double eps, torch::Tensor out);
+unsigned long long bounds_status_gemm();
+unsigned long long bounds_status_gemm_persistent();
+unsigned long long bounds_status_attention();
+unsigned long long bounds_status_attention_tc();
+unsigned long long bounds_status_elementwise();
+unsigned long long bounds_status_sampling();
+unsigned long long bounds_status_comm();
+
+// First bounds violation recorded since the last call (0: none), in the
+// checked build: code << 48 | value; every file's word is read and cleared.
+int64_t bounds_check_status() {
+  unsigned long long first = 0;
+  for (auto fn : {bounds_status_gemm, bounds_status_gemm_persistent, bounds_status_attention, bounds_status_attention_tc, bounds_status_elementwise, bounds_status_sampling, bounds_status_comm}) {
+    const unsigned long long v = fn();
+    if (first == 0) first = v;
+  }
+  return (int64_t)first;
+}
+bool bounds_check_enabled() {
+#ifdef BRAID_BOUNDS_CHECK
+  return true;
+#else
+  return false;
+#endif
+}
 int64_t sp_reduce_allgather(torch::Tensor peers, int64_t recv_off, int64_t rs_flags_off, int64_t ag_flags_off,
                             int64_t g_off, int64_t rstd_off, int64_t rank, int64_t tp, int64_t rpr, int64_t T,
                             int64_t H, int64_t rs_expected, double eps, torch::Tensor status, double timeout_s);
@@ -81,6 +106,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("sin"), py::arg("Hq"), py::arg("Hkv"), py::arg("D"), py::arg("use_rope"),
         py::arg("rs_vec") = py::none(), py::arg("sp") = py::none());
   m.def("row_rstd", &braid::row_rstd, "out[t] = 1/rms(x[t]) in fp32");
+  m.def("bounds_check_status", &braid::bounds_check_status,
+        "checked build: first recorded bounds violation (code << 48 | value), cleared; 0 = none");
+  m.def("bounds_check_enabled", &braid::bounds_check_enabled, "true in the -DBRAID_BOUNDS_CHECK build");
   m.def("sp_reduce_allgather", &braid::sp_reduce_allgather,
         "sequence-parallel reduce of pushed partial rows + all-gather of the new rows and their 1/rms");
   m.def("sp_wait", &braid::sp_wait, "bounded wait for every owner's all-gather");

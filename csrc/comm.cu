@@ -357,3 +357,8 @@ torch::Tensor comm_tensor(int64_t ptr, int64_t offset, std::vector<int64_t> shap
 }
 
 }  // namespace braid
+
+// status word of this file's kernels (checked build; 0 otherwise)
+namespace braid {
+BRAID_BOUNDS_READER(bounds_status_comm)
+}  // namespace braid

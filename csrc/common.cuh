@@ -12,6 +12,39 @@
 
 namespace braid {
 
+// ---- bounds-checked build (-DBRAID_BOUNDS_CHECK; python setup.py with
+// BRAID_BOUNDS_CHECK=1 builds it as braidinfer_b200._C_checked).  Indices that
+// kernels take from data (KV slots, RoPE positions, page ids) are checked
+// before use: a violation records {code << 48 | value} in this translation
+// unit's status word (first violation wins) and the access is skipped or
+// clamped, never trapped, so the context stays usable.  Codes: 1 KV slot
+// outside the cache, 2 position outside the RoPE table, 4 page id outside the
+// KV pool.  In the regular build the checks compile to nothing.
+#ifdef BRAID_BOUNDS_CHECK
+static __device__ unsigned long long g_bounds_status;
+BRAID_DEVICE bool bounds_ok(bool ok, unsigned code, long long value) {
+  if (!ok)
+    atomicCAS(&g_bounds_status, 0ull,
+              ((unsigned long long)code << 48) | ((unsigned long long)value & 0xFFFFFFFFFFFFull));
+  return ok;
+}
+#define BRAID_IN_BOUNDS(cond, code, value) ::braid::bounds_ok((cond), (code), (long long)(value))
+// Host reader of this translation unit's status word: waits for the device,
+// returns the word and clears it.
+#define BRAID_BOUNDS_READER(fn)                                                             \
+  unsigned long long fn() {                                                                 \
+    unsigned long long v = 0, z = 0;                                                        \
+    C10_CUDA_CHECK(cudaDeviceSynchronize());                                                \
+    C10_CUDA_CHECK(cudaMemcpyFromSymbol(&v, ::braid::g_bounds_status, sizeof(v)));         \
+    C10_CUDA_CHECK(cudaMemcpyToSymbol(::braid::g_bounds_status, &z, sizeof(z)));           \
+    return v;                                                                               \
+  }
+#else
+#define BRAID_IN_BOUNDS(cond, code, value) true
+#define BRAID_BOUNDS_READER(fn) \
+  unsigned long long fn() { return 0; }
+#endif
+
 BRAID_DEVICE float bf2f(__nv_bfloat16 x) { return __bfloat162float(x); }
 BRAID_DEVICE __nv_bfloat16 f2bf(float x) { return __float2bfloat16_rn(x); }
 // Round-trip through bf16 (emulates an HF op boundary in bf16).

@@ -118,7 +118,7 @@ __global__ void __launch_bounds__(128) qkv_prepare_kernel(
     __nv_bfloat16* __restrict__ q_out, const __nv_bfloat16* __restrict__ qkv, const int* __restrict__ positions,
     const int* __restrict__ slots, __nv_bfloat16* __restrict__ kv, const __nv_bfloat16* __restrict__ qn,
     const __nv_bfloat16* __restrict__ kn, float eps, const float* __restrict__ cos, const float* __restrict__ sin,
-    int Hq, int Hkv, int PS, int use_rope, int ld_qkv) {
+    int Hq, int Hkv, int PS, int use_rope, int ld_qkv, int num_slots, int rope_len) {
   constexpr int E = D / 32;
   const int t = blockIdx.x;
   const int head = blockIdx.y * 4 + (threadIdx.x >> 5);
@@ -146,7 +146,8 @@ __global__ void __launch_bounds__(128) qkv_prepare_kernel(
     return;
   }
   if (is_k && use_rope) {
-    const int pos = positions[t];
+    int pos = positions[t];
+    if (!BRAID_IN_BOUNDS(pos >= 0 && pos < rope_len, 2, pos)) pos = 0;
     float partner[E];
 #pragma unroll
     for (int j = 0; j < E; ++j) partner[j] = __shfl_xor_sync(0xffffffffu, v[j], 16);
@@ -159,6 +160,7 @@ __global__ void __launch_bounds__(128) qkv_prepare_kernel(
     }
   }
   const int slot = slots[t];
+  if (!BRAID_IN_BOUNDS(slot >= 0 && slot < num_slots, 1, slot)) return;
   const int page = slot / PS, off = slot % PS;
   const int kh = is_k ? head - Hq : head - Hq - Hkv;
   __nv_bfloat16* dst = kv + ((((size_t)page * 2 + (is_k ? 0 : 1)) * Hkv + kh) * PS + off) * D + lane * E;
@@ -248,14 +250,21 @@ void qkv_prepare(torch::Tensor q_out, torch::Tensor qkv, torch::Tensor positions
   if (D == 128)
     qkv_prepare_kernel<128><<<grid, 128, 0, st>>>(bpm(q_out), bp(qkv), positions.data_ptr<int>(), slots.data_ptr<int>(),
                                                   bpm(kv), qn, kn, (float)eps, cos.data_ptr<float>(),
-                                                  sin.data_ptr<float>(), Hq, Hkv, PS, use_rope, qkv.stride(0));
+                                                  sin.data_ptr<float>(), Hq, Hkv, PS, use_rope, qkv.stride(0),
+                                                  (int)(kv.size(0) * PS), (int)cos.size(0));
   else if (D == 64)
     qkv_prepare_kernel<64><<<grid, 128, 0, st>>>(bpm(q_out), bp(qkv), positions.data_ptr<int>(), slots.data_ptr<int>(),
                                                  bpm(kv), qn, kn, (float)eps, cos.data_ptr<float>(),
-                                                 sin.data_ptr<float>(), Hq, Hkv, PS, use_rope, qkv.stride(0));
+                                                 sin.data_ptr<float>(), Hq, Hkv, PS, use_rope, qkv.stride(0),
+                                                  (int)(kv.size(0) * PS), (int)cos.size(0));
   else
     TORCH_CHECK(false, "qkv_prepare: head_dim must be 64 or 128");
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+}  // namespace braid
+
+// status word of this file's kernels (checked build; 0 otherwise)
+namespace braid {
+BRAID_BOUNDS_READER(bounds_status_elementwise)
 }  // namespace braid

@@ -247,3 +247,8 @@ void row_rstd(torch::Tensor x, double eps, torch::Tensor out) {
 }
 
 }  // namespace braid
+
+// status word of this file's kernels (checked build; 0 otherwise)
+namespace braid {
+BRAID_BOUNDS_READER(bounds_status_gemm_persistent)
+}  // namespace braid

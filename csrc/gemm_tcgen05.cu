@@ -76,7 +76,8 @@ BRAID_DEVICE void qkv_head_store(const QkvEpi& q, float* v, int head, int t, int
     return;
   }
   if (is_k && q.use_rope) {
-    const int pos = q.positions[t];
+    int pos = q.positions[t];
+    if (!BRAID_IN_BOUNDS(pos >= 0 && pos < q.rope_len, 2, pos)) pos = 0;
     float pr[E];
 #pragma unroll
     for (int i = 0; i < E; ++i) pr[i] = __shfl_xor_sync(0xffffffffu, v[i], 16);
@@ -89,6 +90,7 @@ BRAID_DEVICE void qkv_head_store(const QkvEpi& q, float* v, int head, int t, int
     }
   }
   const int slot = q.slots[t];
+  if (!BRAID_IN_BOUNDS(slot >= 0 && slot < q.num_slots, 1, slot)) return;
   const int page = slot / q.PS, off = slot % q.PS;
   const int kh = is_k ? head - q.Hq : head - q.Hq - q.Hkv;
   __nv_bfloat16* dst =
@@ -1059,6 +1061,8 @@ void gemm_qkv(torch::Tensor q_out, torch::Tensor x, torch::Tensor w, c10::option
   q.PS = kv.size(3);
   q.use_rope = use_rope ? 1 : 0;
   q.eps = (float)head_eps;
+  q.num_slots = (int)(kv.size(0) * kv.size(3));
+  q.rope_len = (int)cos.size(0);
   if (rs_vec.has_value() && rs_vec->defined()) {
     TORCH_CHECK(rs_vec->scalar_type() == at::kFloat && rs_vec->numel() >= x.size(0), "gemm_qkv: rs_vec");
     a.rs_vec = rs_vec->data_ptr<float>();
@@ -1299,3 +1303,8 @@ extern "C" int braid_gemm_noalloc(void* out, const void* x, const void* w, const
   if (e != cudaSuccess) return fail(9, cudaGetErrorString(e));
   return 0;
 }
+
+// status word of this file's kernels (checked build; 0 otherwise)
+namespace braid {
+BRAID_BOUNDS_READER(bounds_status_gemm)
+}  // namespace braid

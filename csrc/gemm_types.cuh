@@ -23,6 +23,8 @@ struct QkvEpi {
   const float* sin;
   int Hq, Hkv, D, PS, use_rope;
   float eps;
+  int num_slots;  // pages * PS of the cache (checked build)
+  int rope_len;   // rows of cos/sin (checked build)
 };
 
 // Push epilogue (epi == 3, swapped mode): the bf16 result tile is written to
@@ -269,10 +271,12 @@ BRAID_DEVICE void store_tile_normal(const GemmArgs& args, int m0, int n0, int r,
         } else {
           const int slot = q.slots[m];
           const int kh = is_k ? head - q.Hq : head - q.Hq - q.Hkv;
-          dst = q.kv + ((((size_t)(slot / q.PS)) * 2 + (is_k ? 0 : 1)) * q.Hkv + kh) * q.PS * (size_t)D +
-                (size_t)(slot % q.PS) * D;
+          if (BRAID_IN_BOUNDS(slot >= 0 && slot < q.num_slots, 1, slot))
+            dst = q.kv + ((((size_t)(slot / q.PS)) * 2 + (is_k ? 0 : 1)) * q.Hkv + kh) * q.PS * (size_t)D +
+                  (size_t)(slot % q.PS) * D;
         }
         pos = q.positions[m];
+        if (is_k && q.use_rope && !BRAID_IN_BOUNDS(pos >= 0 && pos < q.rope_len, 2, pos)) pos = 0;
       }
       for (int c = 0; c < D / 2; c += 16) {
         float a[16], b[16];

@@ -481,3 +481,8 @@ void tp_sample(torch::Tensor out, torch::Tensor logits, int64_t vocab_start, int
 }
 
 }  // namespace braid
+
+// status word of this file's kernels (checked build; 0 otherwise)
+namespace braid {
+BRAID_BOUNDS_READER(bounds_status_sampling)
+}  // namespace braid

@@ -19,10 +19,19 @@ NVCC = ["-O3", "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-std=
         "-U__CUDA_NO_HALF_CONVERSIONS__", "-U__CUDA_NO_BFLOAT162_OPERATORS__"]
 if os.environ.get("BRAID_PTXAS_V"):
     NVCC.append("-Xptxas=-v")
+CXX = ["-O3", "-std=c++17"]
+# BRAID_BOUNDS_CHECK=1 builds the bounds-checked variant braidinfer_b200._C_checked
+# (indices read from data are checked in the kernels; violations are recorded,
+# not trapped).  Build it into its own temp directory:
+#     BRAID_BOUNDS_CHECK=1 python setup.py build_ext --inplace --build-temp build/checked
+CHECKED = os.environ.get("BRAID_BOUNDS_CHECK") == "1"
+NAME = "braidinfer_b200._C_checked" if CHECKED else "braidinfer_b200._C"
+if CHECKED:
+    NVCC.append("-DBRAID_BOUNDS_CHECK")
+    CXX.append("-DBRAID_BOUNDS_CHECK")
 
 setup(
     name="braidinfer_b200",
-    ext_modules=[CUDAExtension("braidinfer_b200._C", SRC,
-                               extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC})],
+    ext_modules=[CUDAExtension(NAME, SRC, extra_compile_args={"cxx": CXX, "nvcc": NVCC})],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
 )
