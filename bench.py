@@ -13,6 +13,12 @@ the same K steps timed on the host through the public engine API
 (``LLM.step``), which includes each step's host->device metadata upload from
 pinned memory and the device->host read of the sampled tokens.  Weights
 (16 GB) exceed L2 (126 MB) so no flush is needed between steps.
+
+The default 1-GPU run (no --model / --batch) then measures secondary points of
+the baseline configurations the same way and adds them under
+``other_configs``: Qwen3-0.6B bs1/bs8 (k_norm weights up to |w| = 100),
+TinyLlama-1.1B bs8, Llama-3-8B bs1/bs32 (64 timed steps each) and the
+TinyLlama cached-chunk TTFT.  ``--no-extras`` skips them.
 """
 from __future__ import annotations
 
@@ -45,8 +51,11 @@ def parse():
                          "chunk under concurrent queries (Llama-3-70B TP8 config)")
     ap.add_argument("--ctx-len", type=int, default=8192, help="cascade: shared context chunk tokens")
     ap.add_argument("--query-len", type=int, default=256, help="cascade: tokens per query")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="1-GPU default run: skip the secondary configuration points (other models, batches, TTFT)")
     a = ap.parse_args()
     a.model_given = any(x == "--model" or x.startswith("--model=") for x in sys.argv[1:])
+    a.batch_given = any(x == "--batch" or x.startswith("--batch=") for x in sys.argv[1:])
     return a
 
 
@@ -249,11 +258,80 @@ def run_ours(args) -> None:
             "gpu_launches_per_step": launches,
             "impl": "ours",
         }
-        print(json.dumps(line), flush=True)
     llm.exit()
+    if rank == 0 and n == 1 and not (args.no_extras or args.model_given or args.batch_given):
+        del llm, runner
+        line["other_configs"] = measure_extras(args)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     if n > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+# Secondary points of the baseline configurations, measured on one GPU after
+# the headline (same timing rules: warm-up steps, CUDA events around each
+# graph-replayed step, host wall time through LLM.step for e2e).
+EXTRA_POINTS = [  # label, model, batch, prompt tokens, Qwen3 k_norm init bound
+    ("qwen3-0.6b bs1 (k_norm |w|<=100)", "qwen3-0.6b", 1, 512, 100.0),
+    ("qwen3-0.6b bs8 (k_norm |w|<=100)", "qwen3-0.6b", 8, 512, 100.0),
+    ("tinyllama-1.1b bs8", "tinyllama-1.1b", 8, 2048, None),
+    ("llama3-8b bs1", "llama3-8b", 1, 2048, None),
+    ("llama3-8b bs32", "llama3-8b", 32, 2048, None),
+]
+
+
+def _free_gpu() -> None:
+    import gc
+
+    import torch
+
+    gc.collect()
+    torch.cuda.empty_cache()
+
+
+def measure_decode_point(model: str, batch: int, plen: int, steps: int, warmup: int, k_norm=None) -> dict:
+    import types
+
+    from braidinfer_b200 import LLM, SamplingParams
+
+    cfg_dir = make_config_dir(model, with_weights=False)
+    max_len = plen + warmup + steps + 64
+    page = 256
+    kw = dict(init_k_norm_range=k_norm) if k_norm is not None else {}
+    llm = LLM(cfg_dir, load_weights=False, max_num_seqs=batch, max_model_len=max_len,
+              num_kvcache_blocks=batch * (-(-max_len // page)) + 8, kvcache_block_size=page,
+              max_graph_batch=batch, max_num_batched_tokens=max(16384, max_len), **kw)
+    sp = SamplingParams(temperature=0.0, max_tokens=warmup + steps + 4, ignore_eos=True)
+    for p in prompts_for(batch, plen, llm.config.spec.vocab_size):
+        llm.add_request(p, sp)
+    while llm.scheduler.waiting:
+        llm.step()
+    a = types.SimpleNamespace(warmup=warmup, steps=steps, batch=batch)
+    dev_ms, wall, launches, clocks = timed_decode(llm, a, 1)
+    llm.exit()
+    toks = batch * steps
+    return {"value": round(toks / (dev_ms / 1e3), 2), "unit": "tokens/s", "ms_per_step": round(dev_ms / steps, 4),
+            "e2e": round(toks / wall, 2), "steps": steps, "warmup": warmup, "prompt_len": plen,
+            "gpu_launches_per_step": launches, "clocks": clocks.summary()}
+
+
+def measure_extras(args) -> dict:
+    out = {}
+    for label, model, batch, plen, k_norm in EXTRA_POINTS:
+        _free_gpu()
+        try:
+            out[label] = measure_decode_point(model, batch, plen, 64, 8, k_norm)
+        except Exception as e:  # noqa: BLE001 - a secondary point never breaks the headline line
+            out[label] = {"error": f"{type(e).__name__}: {e}"[:300]}
+    _free_gpu()
+    try:
+        import types
+
+        out["tinyllama-1.1b TTFT, cached chunks"] = measure_ttft(types.SimpleNamespace(model_given=False, steps=24))
+    except Exception as e:  # noqa: BLE001
+        out["tinyllama-1.1b TTFT, cached chunks"] = {"error": f"{type(e).__name__}: {e}"[:300]}
+    return out
 
 
 # ------------------------------------------------------------------ cascade
@@ -356,6 +434,10 @@ def run_reference(args) -> None:
 
 # ------------------------------------------------------------------ TTFT
 def run_ttft(args) -> None:
+    print(json.dumps(measure_ttft(args)), flush=True)
+
+
+def measure_ttft(args) -> dict:
     """TTFT of a RAG-style composition: a 128-token system chunk plus 3 of 16
     registered 1024-token contexts plus a 64-token query (the cascade/RAG configuration,
     TinyLlama-1.1B architecture), with the chunks' KV cached, against a full
@@ -410,12 +492,13 @@ def run_ttft(args) -> None:
     if graphs:
         g = graphs[min(graphs)]
         dev_ms = min(timed(g.graph.replay) for _ in range(10))
-    print(json.dumps({"metric": f"TTFT ms with cached chunks ({model}, 128+3x1024 cached + 64 query)",
+    cl.llm.exit()
+    return ({"metric": f"TTFT ms with cached chunks ({model}, 128+3x1024 cached + 64 query)",
                       "value": round(c_ms, 3), "unit": "ms", "higher_is_better": False, "n_gpus": 1,
                       "device_prefill_graph_ms": round(dev_ms, 3) if dev_ms is not None else None,
                       "full_prefill_ms": round(f_ms, 3), "speedup_vs_full_prefill": round(f_ms / c_ms, 2),
                       "dtype": "bf16", "data": "synthetic token ids (seed 2), random-init weights",
-                      "impl": "ours"}), flush=True)
+                      "impl": "ours"})
 
 
 def main():

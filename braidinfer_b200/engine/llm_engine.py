@@ -101,6 +101,10 @@ class LLMEngine:
             return
         self._closed = True
         try:
+            atexit.unregister(self.exit)  # a closed engine can be freed (weights, KV pool)
+        except Exception:
+            pass
+        try:
             self.release_all_retained_sequences()
             # graphs may hold NCCL calls (TP): release them before the process group goes away
             self.model_runner.graphs.clear()
