@@ -66,6 +66,12 @@ ARCH = {
     "tinyllama-1.1b": dict(hidden_size=2048, num_hidden_layers=22, num_attention_heads=32, num_key_value_heads=4,
                            head_dim=64, intermediate_size=5632, vocab_size=32000, rms_norm_eps=1e-5,
                            rope_theta=10000.0, max_position_embeddings=4096),
+    # Qwen3: per-head q_norm / k_norm (k_norm weights drawn with |w| up to 100,
+    # the benchmark configuration's extreme-weight case)
+    "qwen3-0.6b": dict(hidden_size=1024, num_hidden_layers=28, num_attention_heads=16, num_key_value_heads=8,
+                       head_dim=128, intermediate_size=3072, vocab_size=151936, rms_norm_eps=1e-6,
+                       rope_theta=1000000.0, max_position_embeddings=40960, model_type="qwen3",
+                       tie_word_embeddings=True, k_norm_range=100.0),
 }
 
 
@@ -124,19 +130,24 @@ def write_checkpoint(path: str, model: str, tp: int = 1, seed: int = 0) -> str:
         return path
     os.makedirs(path, exist_ok=True)
     a = dict(ARCH[model])
+    model_type = a.pop("model_type", "llama")
+    tie = a.pop("tie_word_embeddings", False)
+    k_norm_range = a.pop("k_norm_range", None)
     H, D, L, V = a["hidden_size"], a["head_dim"], a["num_hidden_layers"], a["vocab_size"]
     nh, nkv, inter = a["num_attention_heads"] // tp, a["num_key_value_heads"] // tp, a["intermediate_size"] // tp
     assert nh * tp == a["num_attention_heads"] and nkv * tp == a["num_key_value_heads"], "heads must divide by tp"
-    cfg = dict(a, num_attention_heads=nh, num_key_value_heads=nkv, intermediate_size=inter, model_type="llama",
-               architectures=["LlamaForCausalLM"], torch_dtype="bfloat16", bos_token_id=1, eos_token_id=2,
-               hidden_act="silu", attention_bias=False, tie_word_embeddings=False)
+    arch = {"llama": "LlamaForCausalLM", "qwen3": "Qwen3ForCausalLM"}[model_type]
+    cfg = dict(a, num_attention_heads=nh, num_key_value_heads=nkv, intermediate_size=inter, model_type=model_type,
+               architectures=[arch], torch_dtype="bfloat16", bos_token_id=1, eos_token_id=2,
+               hidden_act="silu", attention_bias=False, tie_word_embeddings=tie)
     with open(os.path.join(path, "config.json"), "w") as f:
         json.dump(cfg, f, indent=1)
     _write_tokenizer(path, V)
     # A pool of N(0, 0.02) bf16 values; each tensor reads it from a random offset.
     g = torch.Generator().manual_seed(seed)
-    pool = (torch.randn(1 << 27, generator=g) * 0.02).to(torch.bfloat16).view(torch.int16).numpy().tobytes()
-    ones = torch.ones(1 << 16, dtype=torch.bfloat16).view(torch.int16).numpy().tobytes()
+    # host tensors: the reference makes CUDA the default device once its engine exists
+    pool = (torch.randn(1 << 27, generator=g, device="cpu") * 0.02).to(torch.bfloat16).view(torch.int16).numpy().tobytes()
+    ones = torch.ones(1 << 16, dtype=torch.bfloat16, device="cpu").view(torch.int16).numpy().tobytes()
     state = {"pos": 0}
 
     def rnd(n):
@@ -147,6 +158,10 @@ def write_checkpoint(path: str, model: str, tp: int = 1, seed: int = 0) -> str:
     def one(n):
         return ones[:2 * n]
 
+    def k_norm(n):
+        w = (torch.rand(n, generator=g, device="cpu") * 2 - 1) * (k_norm_range or 1.0)
+        return w.to(torch.bfloat16).view(torch.int16).numpy().tobytes()
+
     ts = [("model.embed_tokens.weight", (V, H), rnd)]
     for i in range(L):
         p = f"model.layers.{i}."
@@ -155,6 +170,10 @@ def write_checkpoint(path: str, model: str, tp: int = 1, seed: int = 0) -> str:
                (p + "self_attn.v_proj.weight", (nkv * D, H), rnd), (p + "self_attn.o_proj.weight", (H, nh * D), rnd),
                (p + "mlp.gate_proj.weight", (inter, H), rnd), (p + "mlp.up_proj.weight", (inter, H), rnd),
                (p + "mlp.down_proj.weight", (H, inter), rnd)]
+        if model_type == "qwen3":
+            ts += [(p + "self_attn.q_norm.weight", (D,), one),
+                   (p + "self_attn.k_norm.weight", (D,), k_norm if k_norm_range else one)]
+    # the reference's Qwen3 has its own lm_head parameter (no tying), so the head is always written
     ts += [("model.norm.weight", (H,), one), ("lm_head.weight", (V, H), rnd)]
     _stream_safetensors(os.path.join(path, "model.safetensors"), ts)
     return path
@@ -286,7 +305,43 @@ def run_tp1(args, clock_sampler, published: float) -> None:
         clocks.mark(e0, time.time())
     note = ("reference cannot batch (NotImplementedError for batch > 1): requests decoded one at a time, "
             "a lower bound; transformers-5.5 rope_scaling shim applied to AutoConfig in this process")
-    print(json.dumps(_line(args, 1, dev_ms, wall, toks, clocks.summary(), published, note)), flush=True)
+    line = _line(args, 1, dev_ms, wall, toks, clocks.summary(), published, note)
+    if not (getattr(args, "no_extras", False) or getattr(args, "model_given", False) or
+            getattr(args, "batch_given", False)):
+        line["other_configs"] = _extras(LLM, SamplingParams)
+    print(json.dumps(line), flush=True)
+
+
+# Secondary points of the baseline configurations that the reference can run
+# (same labels as the other arm's ``other_configs``).
+REF_EXTRAS = [  # label, model, batch, prompt tokens, warm-up, timed steps
+    ("qwen3-0.6b bs1 (k_norm |w|<=100)", "qwen3-0.6b", 1, 512, 8, 64),
+    ("tinyllama-1.1b bs8", "tinyllama-1.1b", 8, 2048, 4, 32),
+]
+
+
+def _extras(LLM, SamplingParams) -> dict:
+    import tempfile
+    import types
+
+    out = {}
+    for label, model, batch, plen, warmup, steps in REF_EXTRAS:
+        try:
+            d = write_checkpoint(os.path.join(tempfile.gettempdir(), f"braid_ref_{model}_tp1"), model)
+            a = types.SimpleNamespace(prompt_len=plen, warmup=warmup, steps=steps)
+            with contextlib.redirect_stdout(io.StringIO()):
+                llm = LLM(d, **_engine_kwargs(a))
+            sp = SamplingParams(temperature=0.0, max_tokens=warmup + steps + 3, ignore_eos=True)
+            dev_ms, wall, toks = _decode_requests(llm, _prompts(batch, plen, ARCH[model]["vocab_size"]), sp,
+                                                  warmup, steps)
+            out[label] = {"value": round(toks / (dev_ms / 1e3), 2), "unit": "tokens/s",
+                          "ms_per_step": round(dev_ms / toks, 4), "e2e": round(toks / wall, 2), "steps": steps,
+                          "warmup": warmup, "prompt_len": plen,
+                          "note": "requests decoded one at a time (the reference cannot batch)"}
+            del llm
+        except Exception as e:  # noqa: BLE001 - a secondary point never breaks the headline line
+            out[label] = {"error": f"{type(e).__name__}: {e}"[:300]}
+    return out
 
 
 def run_tp(args, clock_sampler, published: float) -> None:

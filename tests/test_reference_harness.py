@@ -100,3 +100,24 @@ def test_tp_build_uses_reference_all_reduce(tmp_path):
         assert name == "RowParallelLocalShard"
         assert o_shape == (256, 128) and down_shape == (256, 344)
         assert ok, f"rank {rank}: row-parallel output is not the all-reduced sum"
+
+
+def test_qwen3_checkpoint_has_head_norms_with_extreme_k_norm(tmp_path):
+    """The reference arm's Qwen3 checkpoint: per-head q_norm / k_norm tensors,
+    k_norm drawn up to |w| = 100, the reference's own lm_head written out."""
+    h = _harness()
+    h.ARCH.setdefault("tiny-qwen3", dict(TINY, model_type="qwen3", tie_word_embeddings=True, k_norm_range=100.0))
+    d = h.write_checkpoint(str(tmp_path / "q3"), "tiny-qwen3", seed=2)
+    import json
+
+    from safetensors import safe_open
+
+    cfg = json.load(open(os.path.join(d, "config.json")))
+    assert cfg["model_type"] == "qwen3" and cfg["architectures"] == ["Qwen3ForCausalLM"]
+    assert "k_norm_range" not in cfg
+    with safe_open(os.path.join(d, "model.safetensors"), "pt", "cpu") as f:
+        kn = f.get_tensor("model.layers.1.self_attn.k_norm.weight").float()
+        qn = f.get_tensor("model.layers.0.self_attn.q_norm.weight").float()
+        assert "lm_head.weight" in f.keys()
+    assert kn.shape == (64,) and 50 < kn.abs().max().item() <= 100
+    assert torch.equal(qn, torch.ones(64))
