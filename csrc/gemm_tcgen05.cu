@@ -818,6 +818,10 @@ static void split_plan(int tiles, int kb_total, int BN, bool swap, int& splits, 
   const int slots = gemm_num_sms() * (swap ? 2 : 1);
   if (tiles < slots) splits = std::max(1, std::min({slots / tiles, kb_total / 2, 16}));
   splits = std::max(1, std::min(splits, 256 / BN));
+  // With 16+ output tiles, more than 8 slices measured slower on B200 (the last
+  // CTA's sum of 9-16 partials outweighs the extra streams); only a handful
+  // of tiles needs up to 16 slices to fill the machine.
+  if (tiles >= 16) splits = std::min(splits, 8);
   const int forced = g_forced_splits >= 0 ? g_forced_splits : [] {  // BRAID_GEMM_SPLITS=n forces the factor
     static const int env = [] {
       const char* e = getenv("BRAID_GEMM_SPLITS");
@@ -1276,6 +1280,7 @@ extern "C" int braid_gemm_noalloc(void* out, const void* x, const void* w, const
   const int slots = gemm_num_sms() * 2;
   if (tiles < slots) splits = std::max(1, std::min({slots / tiles, kb_total / 2, 16}));
   splits = std::max(1, std::min(splits, 256 / BN));
+  if (tiles >= 16) splits = std::min(splits, 8);
   // ... and never more partial space than the fixed array holds
   while (splits > 1 && (size_t)tiles * splits * BM * BN * 4 > BRAID_NOALLOC_PARTIAL_BYTES) --splits;
   int kbps = (kb_total + splits - 1) / splits;
