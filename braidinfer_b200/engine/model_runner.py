@@ -59,6 +59,8 @@ class _GraphSlot:
         self.page_cap = 0
         self.num_splits = 1
         self.launches = 0
+        self.dev_all = None  # device buffer of fbuf / ibuf / lbuf / meta_buf (views)
+        self.pin_all = None  # its pinned host mirror (pin_l / pin_f / pin_k / pin_meta are numpy views)
         self.pin_meta = self.pin_f = self.pin_k = self.pin_l = self.pin_out = self.pin_status = None
 
 
@@ -343,7 +345,17 @@ class ModelRunner:
             plan = build_plan([], self.page_size, pad_seqs=B, scratch_page=pm.scratch_page,
                               seg_cap=g.seg_cap, page_cap=g.page_cap, group=(0, set()) if shared else None)
         g.sizes = plan.sizes
-        g.meta_buf = torch.from_numpy(pack(plan)).to(self.device)
+        # One device buffer holds the step's sampling settings and packed plan
+        # (int64 [2, B] | float32 [3, B] | int32 [B] | int32 plan), so a replay
+        # uploads them with ONE host->device copy from a pinned mirror.
+        packed0 = pack(plan)
+        nl, nf, nk = 16 * B, 12 * B, 4 * B
+        g.dev_all = torch.zeros(nl + nf + nk + 4 * packed0.size, dtype=torch.uint8, device=self.device)
+        g.lbuf = g.dev_all[:nl].view(torch.int64).view(2, B)
+        g.fbuf = g.dev_all[nl:nl + nf].view(torch.float32).view(3, B)
+        g.ibuf = g.dev_all[nl + nf:nl + nf + nk].view(torch.int32)
+        g.meta_buf = g.dev_all[nl + nf + nk:].view(torch.int32)
+        g.meta_buf.copy_(torch.from_numpy(packed0))
         views = unpack(g.meta_buf, g.sizes)
         g.num_splits = 1 if prefill_tokens else self._decode_splits(B)
         meta = make_meta(views, plan, g.num_splits,
@@ -351,10 +363,7 @@ class ModelRunner:
         meta.decode = not prefill_tokens
         meta.max_q_len = prefill_tokens or 1
         meta.max_kv_len = self.config.max_model_len
-        g.fbuf = torch.zeros(3, B, dtype=torch.float32, device=self.device)
         g.fbuf[1].fill_(1.0)
-        g.ibuf = torch.zeros(B, dtype=torch.int32, device=self.device)
-        g.lbuf = torch.zeros(2, B, dtype=torch.int64, device=self.device)
         g.out = torch.zeros(B, dtype=torch.int32, device=self.device)
         kv = pm.kv_cache
 
@@ -419,6 +428,14 @@ class ModelRunner:
             g = table.get(B)
             if g is None:
                 g = table[B] = self._capture(B, tp_sampling=tps)
+        plain = items is None and group is None
+        spec, self._spec = getattr(self, "_spec", None), None
+        if plain and spec is not None and spec[0] is g and spec[1] == self._decode_key(seqs, 0):
+            # this step's plan was built while the previous step ran on the GPU;
+            # only the sampled tokens (input ids lead the packed plan) are new
+            packed = spec[2]
+            packed[:len(seqs)] = [s.token_ids[-1] for s in seqs]
+            return self._replay(g, packed, seqs, B, speculate=True)
         try:
             plan = build_plan(items if items is not None else self._items_for(seqs), self.page_size,
                               pad_seqs=B - len(seqs), scratch_page=self.page_manager.scratch_page,
@@ -427,7 +444,34 @@ class ModelRunner:
             return None
         if plan.sizes != g.sizes:
             return None
-        return self._replay(g, plan, seqs, B)
+        return self._replay(g, pack(plan), seqs, B, speculate=plain)
+
+    @staticmethod
+    def _decode_key(seqs: List[Sequence], ahead: int) -> tuple:
+        """State of a decode batch that a prebuilt plan depends on, ``ahead``
+        steps from now (every sequence one token longer per step)."""
+        return tuple((s.seq_id, s.num_cached_tokens + ahead, s.num_tokens + ahead, s.pos_base, hash(tuple(s.pages)),
+                      tuple(id(sg) for sg in s.segments)) for s in seqs)
+
+    def _speculate(self, g: "_GraphSlot", seqs: List[Sequence], B: int):
+        """The NEXT decode step's packed plan, assuming the same sequences each
+        grow by one token (its id is filled in when the step runs) and no new
+        KV page is needed; None when that cannot be prebuilt."""
+        items = []
+        for s in seqs:
+            L = s.num_tokens
+            if s.num_cached_tokens != L - 1 or L // self.page_size >= len(s.pages):
+                return None
+            items.append(FwdItem(tokens=[0], pos0=s.pos_base + L, priv_index0=L, priv_pages=s.pages,
+                                 priv_pos0=s.pos_base, segments=s.segments, logits=True))
+        try:
+            plan = build_plan(items, self.page_size, pad_seqs=B - len(seqs), scratch_page=self.page_manager.scratch_page,
+                              seg_cap=g.seg_cap, page_cap=g.page_cap)
+        except OverflowError:
+            return None
+        if plan.sizes != g.sizes:
+            return None
+        return (g, self._decode_key(seqs, 1), pack(plan))
 
     def _prefill_bucket(self, n: int) -> int:
         cap = self.config.max_prefill_graph_tokens
@@ -453,32 +497,36 @@ class ModelRunner:
             return None
         if plan.sizes != g.sizes:
             return None
-        return self._replay(g, plan, [seq], 1)
+        return self._replay(g, pack(plan), [seq], 1)
 
-    def _replay(self, g: _GraphSlot, plan, seqs: List[Sequence], B: int) -> List[int]:
+    def _replay(self, g: _GraphSlot, packed: np.ndarray, seqs: List[Sequence], B: int,
+                speculate: bool = False) -> List[int]:
         with nvtx_range(f"graph replay b={B}"):
-            return self._replay_graph(g, plan, seqs, B)
+            return self._replay_graph(g, packed, seqs, B, speculate)
 
-    def _replay_graph(self, g: _GraphSlot, plan, seqs: List[Sequence], B: int) -> List[int]:
+    def _replay_graph(self, g: _GraphSlot, packed: np.ndarray, seqs: List[Sequence], B: int,
+                      speculate: bool) -> List[int]:
+        """Upload the packed plan and sampling settings, replay the captured
+        step, read the tokens back.  ``speculate``: while the GPU runs, prebuild
+        the next decode step's plan (``_speculate``)."""
         # Persistent pinned staging: the previous step's copies completed at its
         # token read-back, so the buffers are free to overwrite.
-        if g.pin_meta is None:
-            g.pin_meta = torch.empty(g.meta_buf.numel(), dtype=torch.int32).pin_memory()
-            g.pin_f = torch.empty(3, B, dtype=torch.float32).pin_memory()
-            g.pin_k = torch.empty(B, dtype=torch.int32).pin_memory()
-            g.pin_l = torch.empty(2, B, dtype=torch.int64).pin_memory()
+        if g.pin_all is None:
+            g.pin_all = torch.empty(g.dev_all.numel(), dtype=torch.uint8).pin_memory()
+            a = g.pin_all.numpy()
+            nl, nf, nk = 16 * B, 12 * B, 4 * B
+            g.pin_l = a[:nl].view(np.int64).reshape(2, B)
+            g.pin_f = a[nl:nl + nf].view(np.float32).reshape(3, B)
+            g.pin_k = a[nl + nf:nl + nf + nk].view(np.int32)
+            g.pin_meta = a[nl + nf + nk:].view(np.int32)
             g.pin_out = torch.empty(B, dtype=torch.int32).pin_memory()
-        packed = pack(plan)
-        g.pin_meta.numpy()[:] = packed
+        g.pin_meta[:] = packed
         f, k, l = self._sampling_tensors(seqs, pad=B - len(seqs))
-        g.pin_f.numpy()[:] = f
-        g.pin_k.numpy()[:] = k
-        g.pin_l.numpy()[:] = l
-        g.meta_buf.copy_(g.pin_meta, non_blocking=True)
-        g.fbuf.copy_(g.pin_f, non_blocking=True)
-        g.ibuf.copy_(g.pin_k, non_blocking=True)
-        g.lbuf.copy_(g.pin_l, non_blocking=True)
-        self.last_h2d_bytes = packed.nbytes + f.nbytes + k.nbytes + l.nbytes
+        g.pin_f[:] = f
+        g.pin_k[:] = k
+        g.pin_l[:] = l
+        g.dev_all.copy_(g.pin_all, non_blocking=True)
+        self.last_h2d_bytes = g.pin_all.numel()
         if self.event_log is not None:
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
@@ -492,6 +540,8 @@ class ModelRunner:
             if g.pin_status is None:
                 g.pin_status = torch.zeros(4, dtype=torch.int32).pin_memory()
             g.pin_status.copy_(self.fused_comm.status, non_blocking=True)
+        if speculate:
+            self._spec = self._speculate(g, seqs, B)
         torch.cuda.current_stream(self.device).synchronize()
         if self.fused_comm is not None and int(g.pin_status[0]) != 0:
             self.fused_comm.check()
