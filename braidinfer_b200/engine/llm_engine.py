@@ -107,6 +107,8 @@ class LLMEngine:
         try:
             self.release_all_retained_sequences()
             # graphs may hold NCCL calls (TP): release them before the process group goes away
+            # (the prebuilt next-step plan refers to its graph slot too)
+            self.model_runner._spec = None
             self.model_runner.graphs.clear()
             self.model_runner.graphs_gather.clear()
             self.model_runner.graphs_shared.clear()

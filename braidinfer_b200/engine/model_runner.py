@@ -95,6 +95,7 @@ class ModelRunner:
         self.sms = _num_sms(self.device)
         self.timing = {"steps": 0, "prefill_tokens": 0, "decode_tokens": 0}
         self.capture_logits: Optional[list] = None  # debug/test hook (eager steps only)
+        self._spec = None  # (graph slot, batch state key, packed plan) of the next decode step
         self.event_log: Optional[list] = None  # (start, end) CUDA events around each graph replay
         self.fused_comm = None  # set when the peer-memory TP runtime is enabled
         self.prefill_graphs: Dict[int, _GraphSlot] = {}
@@ -429,7 +430,7 @@ class ModelRunner:
             if g is None:
                 g = table[B] = self._capture(B, tp_sampling=tps)
         plain = items is None and group is None
-        spec, self._spec = getattr(self, "_spec", None), None
+        spec, self._spec = self._spec, None
         if plain and spec is not None and spec[0] is g and spec[1] == self._decode_key(seqs, 0):
             # this step's plan was built while the previous step ran on the GPU;
             # only the sampled tokens (input ids lead the packed plan) are new
