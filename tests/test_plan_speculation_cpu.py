@@ -5,12 +5,14 @@ page is not prebuilt."""
 import types
 
 import numpy as np
+import pytest
 
 from braidinfer_b200 import LLM, SamplingParams
 from braidinfer_b200.engine.batch import build_plan, pack
 
 
-def test_speculated_plan_equals_next_step_plan(tiny_llama_dir):
+@pytest.mark.parametrize("max_tokens", [(30, 30, 30), (9, 30, 17)], ids=["same", "batch-shrinks"])
+def test_speculated_plan_equals_next_step_plan(tiny_llama_dir, max_tokens):
     llm = LLM(tiny_llama_dir, num_kvcache_blocks=64, kvcache_block_size=16, device="cpu", dtype="float32")
     runner = llm.model_runner
     B = 4
@@ -37,8 +39,10 @@ def test_speculated_plan_equals_next_step_plan(tiny_llama_dir):
         return orig(seqs, is_prefill)
 
     runner.run = run
-    sp = SamplingParams(temperature=0, max_tokens=30, ignore_eos=True)
-    llm.generate([list(range(3, 3 + n)) for n in (5, 20, 31)], sp)
+    sps = [SamplingParams(temperature=0, max_tokens=m, ignore_eos=True) for m in max_tokens]
+    llm.generate([list(range(3, 3 + n)) for n in (5, 20, 31)], sps)
     assert state["decode_steps"] >= 29
     assert state["refused"] >= 3          # page boundaries (16-token pages) are not prebuilt
-    assert state["hits"] >= state["decode_steps"] - state["refused"] - 2
+    # a step after the batch changed (a sequence finished) is rebuilt, not reused
+    shrinks = len(set(max_tokens)) - 1
+    assert state["hits"] >= state["decode_steps"] - state["refused"] - 2 - shrinks
