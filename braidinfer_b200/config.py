@@ -141,6 +141,7 @@ class Config:
     comm_timeout_s: float = 5.0
     heartbeat_every: int = 64      # TP: check peer liveness every N engine steps (0 = off)
     shared_prefix_batching: bool = True  # decode: attend once to segments shared by several sequences
+    validate_plans: bool = False   # check every step's metadata on the host before upload (also BRAID_VALIDATE_PLAN=1)
     seed: int = 0
     load_weights: bool = True     # False: random-init weights (synthetic benchmarks)
     init_std: float = 0.02

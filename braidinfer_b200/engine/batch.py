@@ -205,6 +205,48 @@ def build_plan(items: List[FwdItem], page_size: int, pad_seqs: int = 0, scratch_
     return Plan(arrays, nseq, len(ids), max_q, max_kv, decode=(max_q == 1 and len(ids) == nseq), sizes=sizes)
 
 
+def validate_plan(plan: Plan, page_size: int, num_pages: int, rope_len: Optional[int] = None) -> None:
+    """Host-side check of a step's metadata before it is uploaded: every page
+    id inside the KV pool, every KV slot inside the cache, every position
+    inside the RoPE table, the index arrays non-decreasing, every segment
+    given the pages its keys need.  Raises ``PlanValidationError`` naming the
+    field; a kernel given such a plan would read or write outside its buffers."""
+    from ..errors import PlanValidationError
+
+    a = plan.arrays
+
+    def bad(field: str, what: str):
+        raise PlanValidationError(f"step plan: {field} {what}")
+
+    n = len(a["input_ids"])
+    pids, slots, pos = a["page_ids"], a["slots"], a["positions"]
+    if pids.size and (pids.min() < 0 or pids.max() >= num_pages):
+        bad("page_ids", f"outside the pool [0, {num_pages}): {int(pids.min())}..{int(pids.max())}")
+    if slots.size and (slots.min() < 0 or slots.max() >= num_pages * page_size):
+        bad("slots", f"outside the cache [0, {num_pages * page_size}): {int(slots.min())}..{int(slots.max())}")
+    if rope_len is not None and pos.size and (pos.min() < 0 or pos.max() >= rope_len):
+        bad("positions", f"outside the RoPE table [0, {rope_len}): {int(pos.min())}..{int(pos.max())}")
+    for k in ("qo_indptr", "seg_indptr", "seg_page_indptr"):
+        if a[k].size and (a[k][0] != 0 or np.any(np.diff(a[k]) < 0)):
+            bad(k, "does not start at 0 or decreases")
+    if a["qo_indptr"][-1] > n:
+        bad("qo_indptr", f"ends past the {n} tokens")
+    spi, off, ln = a["seg_page_indptr"], a["seg_offset"], a["seg_len"]
+    if spi[-1] > len(pids):
+        bad("seg_page_indptr", f"ends past the {len(pids)} page ids")
+    if np.any(ln < 0) or np.any(off < 0):
+        bad("seg_len/seg_offset", "negative")
+    if a["seg_indptr"][-1] > len(ln):
+        bad("seg_indptr", f"ends past the {len(ln)} segments")
+    live = ln > 0
+    need = -(-(off + ln) // page_size)
+    if np.any(np.diff(spi)[:len(ln)][live] < need[live]):
+        bad("seg_page_indptr", "gives a segment fewer pages than its keys need")
+    li = a["logits_idx"]
+    if li.size and (li.min() < 0 or li.max() >= n):
+        bad("logits_idx", f"outside the {n} tokens")
+
+
 def _fields(keys) -> tuple:
     return FIELDS + (GROUP_FIELDS if "seq_nsh" in keys else ())
 

@@ -16,6 +16,7 @@ inputs, run model, sample, chunk prefill) re-designed for throughput:
 """
 from __future__ import annotations
 
+import os
 import time
 from typing import Dict, List, Optional, Tuple
 
@@ -28,7 +29,7 @@ from ..models import build_model
 from ..parallel.state import TPState
 from ..utils.logging import get_logger
 from ..utils.tracing import nvtx_range
-from .batch import FwdItem, Plan, build_plan, find_shared_group, make_meta, pack, unpack
+from .batch import FwdItem, Plan, build_plan, find_shared_group, make_meta, pack, unpack, validate_plan
 from .page_manager import PageManager
 from .sequence import Sequence
 
@@ -96,6 +97,7 @@ class ModelRunner:
         self.timing = {"steps": 0, "prefill_tokens": 0, "decode_tokens": 0}
         self.capture_logits: Optional[list] = None  # debug/test hook (eager steps only)
         self._spec = None  # (graph slot, batch state key, packed plan) of the next decode step
+        self.validate = config.validate_plans or os.environ.get("BRAID_VALIDATE_PLAN") == "1"
         self.event_log: Optional[list] = None  # (start, end) CUDA events around each graph replay
         self.fused_comm = None  # set when the peer-memory TP runtime is enabled
         self.prefill_graphs: Dict[int, _GraphSlot] = {}
@@ -166,6 +168,10 @@ class ModelRunner:
         f[1, len(seqs):] = 1.0
         return f, k, l
 
+    def _check_plan(self, plan: Plan) -> None:
+        if self.validate:
+            validate_plan(plan, self.page_size, self.page_manager.num_pages, getattr(self.model, "rope_len", None))
+
     def _to_dev(self, a: np.ndarray) -> torch.Tensor:
         t = torch.from_numpy(a)
         if self.device.type == "cuda":
@@ -176,6 +182,7 @@ class ModelRunner:
         """Eager forward; returns final-normed hidden rows of items with ``logits=True``.
         ``group``: shared-prefix group of a decode batch (members first)."""
         plan = build_plan(items, self.page_size, group=group)
+        self._check_plan(plan)
         views = self._upload(plan)
         ns = self._decode_splits(plan.num_seqs, plan.max_kv_len) if plan.decode else 1
         sh = self._shared_splits(plan.num_seqs, ns) if group is not None and group[0] > 0 else 0
@@ -445,6 +452,7 @@ class ModelRunner:
             return None
         if plan.sizes != g.sizes:
             return None
+        self._check_plan(plan)
         return self._replay(g, pack(plan), seqs, B, speculate=plain)
 
     @staticmethod
@@ -472,6 +480,7 @@ class ModelRunner:
             return None
         if plan.sizes != g.sizes:
             return None
+        self._check_plan(plan)
         return (g, self._decode_key(seqs, 1), pack(plan))
 
     def _prefill_bucket(self, n: int) -> int:
@@ -498,6 +507,7 @@ class ModelRunner:
             return None
         if plan.sizes != g.sizes:
             return None
+        self._check_plan(plan)
         return self._replay(g, pack(plan), [seq], 1)
 
     def _replay(self, g: _GraphSlot, packed: np.ndarray, seqs: List[Sequence], B: int,

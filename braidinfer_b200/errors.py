@@ -27,6 +27,11 @@ class InferenceError(BraidError):
     pass
 
 
+class PlanValidationError(InferenceError):
+    """A step's kernel metadata indexes outside its buffers (raised only with
+    plan validation on: ``Config.validate_plans`` or ``BRAID_VALIDATE_PLAN=1``)."""
+
+
 class OutOfPagesError(BraidError, MemoryError):
     """The paged KV pool has no free page even after eviction and preemption."""
 
