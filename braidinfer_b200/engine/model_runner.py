@@ -459,7 +459,7 @@ class ModelRunner:
     def _decode_key(seqs: List[Sequence], ahead: int) -> tuple:
         """State of a decode batch that a prebuilt plan depends on, ``ahead``
         steps from now (every sequence one token longer per step)."""
-        return tuple((s.seq_id, s.num_cached_tokens + ahead, s.num_tokens + ahead, s.pos_base, hash(tuple(s.pages)),
+        return tuple((s.seq_id, s.num_cached_tokens + ahead, s.num_tokens + ahead, s.pos_base, tuple(s.pages),
                       tuple(id(sg) for sg in s.segments)) for s in seqs)
 
     def _speculate(self, g: "_GraphSlot", seqs: List[Sequence], B: int):
