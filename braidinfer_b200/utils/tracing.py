@@ -5,10 +5,10 @@ environment, or ``tracing.enable()``, every engine step is bracketed by a
 range named for its phase and batch (``decode b=8 t=8``, ``prefill b=1
 t=2048``) and the model runner marks its sub-phases (eager forward, CUDA-graph
 replay, sampling), so a timeline profiler that records NVTX (Nsight Systems,
-``torch.profiler`` with CUDA activities, or ``ncu --nvtx --nvtx-include``)
-shows the device work grouped per engine step.  Ranges are host-side: inside a
-CUDA-graph replay the individual kernels are not annotated, the replay as a
-whole is.
+``ncu --nvtx --nvtx-include``) shows the device work grouped per engine step,
+and a ``torch.profiler`` trace carries the same names as ``record_function``
+events.  Ranges are host-side: inside a CUDA-graph replay the individual
+kernels are not annotated, the replay as a whole is.
 
 The reference has no tracing layer of its own (it relies on external
 profilers and ad-hoc ``time.time()`` prints in its benchmark scripts).
@@ -47,13 +47,18 @@ def _nvtx_calls():
 
 @contextlib.contextmanager
 def nvtx_range(name: str) -> Iterator[None]:
-    """``with nvtx_range("decode b=8"): ...`` — a no-op unless enabled."""
+    """``with nvtx_range("decode b=8"): ...`` — a no-op unless enabled.  When
+    enabled the range is also a ``torch.profiler.record_function`` scope, so
+    the same names label the host events of a ``torch.profiler`` trace."""
     if not _enabled:
         yield
         return
+    import torch
+
     push, pop = _nvtx_calls()
     push(name)
     try:
-        yield
+        with torch.profiler.record_function(name):
+            yield
     finally:
         pop()

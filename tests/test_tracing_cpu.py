@@ -24,3 +24,19 @@ def test_nvtx_ranges_bracket_every_step(tiny_llama_dir):
     assert any(n.startswith("prefill b=") for n in names)
     assert any(n.startswith("decode b=2") for n in names)
     assert "sample" in names and any(n.startswith("forward t=") for n in names)
+
+
+def test_ranges_label_torch_profiler_events(tiny_llama_dir):
+    import torch
+
+    llm = LLM(tiny_llama_dir, num_kvcache_blocks=32, kvcache_block_size=16, device="cpu", dtype="float32")
+    sp = SamplingParams(temperature=0, max_tokens=2, ignore_eos=True)
+    tracing.enable(True, push=lambda n: None, pop=lambda: None)
+    try:
+        with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CPU]) as prof:
+            llm.generate([list(range(3, 20))], sp)
+    finally:
+        tracing.enable(False)
+    names = {e.name for e in prof.events()}
+    assert any(n.startswith("prefill b=1") for n in names)
+    assert any(n.startswith("decode b=1") for n in names) and "sample" in names
