@@ -25,6 +25,7 @@ import torch
 
 from .. import ops
 from ..config import Config
+from ..errors import PlanValidationError
 from ..models import build_model
 from ..parallel.state import TPState
 from ..utils.logging import get_logger
@@ -480,7 +481,10 @@ class ModelRunner:
             return None
         if plan.sizes != g.sizes:
             return None
-        self._check_plan(plan)
+        try:
+            self._check_plan(plan)
+        except PlanValidationError:
+            return None  # not prebuilt; the step's own plan is built and checked when it runs
         return (g, self._decode_key(seqs, 1), pack(plan))
 
     def _prefill_bucket(self, n: int) -> int:
